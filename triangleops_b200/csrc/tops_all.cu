@@ -1,0 +1,4 @@
+// tops_all.cu — unity build of the TriangleOps B200 library: every kernel and
+// C-ABI entry point lives in one translation unit (no relocatable device code).
+#include "common.cu"
+#include "selftest.cu"
