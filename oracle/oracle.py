@@ -1,0 +1,208 @@
+"""CPU fp32 oracle for the TriangleOps hot path — TEST INFRASTRUCTURE ONLY.
+
+This module is the parity checker. Only ``tests/``, ``__graft_entry__.smoke()``
+and ``bench.py``'s CPU-baseline / reference legs may import it, and only to
+check or to time the reference algorithm on the host; the product path
+(``triangleops_b200``) never calls it and has no CPU fallback.
+
+Each function restates, in plain fp32 torch on the CPU, the reference's pure-torch
+implementation of one op (youngchan2/TriangleOps ``benchmarks/references.py``):
+
+* :func:`triangle_attention`              <- ``references.py:174-205``
+* :func:`triangle_attention_chunked`      <- same formula, applied to blocks of pair rows
+* :func:`triangle_multiplicative_update`  <- ``references.py:208-221``
+* :func:`attention_pair_bias`             <- ``references.py:143-171``
+* :func:`attention_pair_bias_masked`      <- ``references.py:224-277`` with ``b_q=0``, no qk-norm
+
+plus the LN-affine fold of ``triangle_ops/_common/ln_absorption.py:28-63``
+(:func:`absorb_ln`, :func:`absorb_ln_matmul`).
+
+Parity pin: ``tests/golden/make_golden.py`` runs the reference's own functions
+(imported from a reference checkout) on seeded inputs and stores inputs and
+outputs under ``tests/golden/``; ``tests/test_oracle_golden.py`` checks this
+module against those fixtures.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+def _f32(*ts):
+    return [None if t is None else t.detach().to("cpu", torch.float32) for t in ts]
+
+
+# --------------------------------------------------------------------------- #
+# LN-affine absorption (triangle_ops/_common/ln_absorption.py)
+# --------------------------------------------------------------------------- #
+def absorb_ln(weight, w_ln, b_ln):
+    """(out,in) weight: Wc = W * w_ln, sumW = rowsum(Wc), Bc = W @ b_ln
+    (``_common/ln_absorption.py:28-44``). All fp32."""
+    Wf, w, b = _f32(weight, w_ln, b_ln)
+    Wc = Wf * w.unsqueeze(0)
+    return Wc, Wc.sum(dim=1), Wf @ b
+
+
+def absorb_ln_matmul(weight, w_ln, b_ln):
+    """(in,out) weight: Wc = W * w_ln[:,None], sumW = colsum(Wc), Bc = b_ln @ W
+    (``_common/ln_absorption.py:47-63``). All fp32."""
+    Wf, w, b = _f32(weight, w_ln, b_ln)
+    Wc = Wf * w.unsqueeze(-1)
+    return Wc, Wc.sum(dim=0), b @ Wf
+
+
+# --------------------------------------------------------------------------- #
+# triangle attention (references.py:174-205)
+# --------------------------------------------------------------------------- #
+def triangle_attention(X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
+                       H, D, scale=1.0, eps=1e-5, mask=None):
+    """Starting-node triangle attention on a (N, N, C) pair tensor, fp32 CPU.
+
+    LN(x) -> Q/K/V = LN(x) @ W (matmul convention), bias Bp[h,q,k] = LN(x)[q,k] @ W_proj_z + B_proj_z,
+    S = (Q*scale) K^T + Bp (+ -1e9 where mask[i,k] is False, ``references.py:200-201``),
+    O = softmax(S) V, gate sigma(LN(x) @ W_g^T) (``references.py:203``), then W_o.
+    """
+    (X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o) = _f32(
+        X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o)
+    N, _, Cin = X.shape
+    xln = F.layer_norm(X, (Cin,), W_ln, B_ln, eps=eps)
+    q = (xln @ WQ).view(N, N, H, D).permute(0, 2, 1, 3)
+    k = (xln @ WK).view(N, N, H, D).permute(0, 2, 1, 3)
+    v = (xln @ WV).view(N, N, H, D).permute(0, 2, 1, 3)
+    bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
+    bp = (xln @ W_proj_z + bz).permute(2, 0, 1).unsqueeze(0)
+    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
+    if mask is not None:
+        m = mask.detach().to("cpu").bool()
+        scores = scores + torch.where(m[:, None, None, :], 0.0, -1e9)
+    o = torch.matmul(torch.softmax(scores, -1), v).permute(0, 2, 1, 3).reshape(N, N, H * D)
+    g = torch.sigmoid(F.linear(xln, W_proj_g, B_proj_g)).view(N, N, H, D)
+    o = (o.view(N, N, H, D) * g).reshape(N, N, H * D)
+    return F.linear(o, W_proj_o, B_proj_o)
+
+
+def triangle_attention_chunked(X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o,
+                               B_proj_o, H, D, scale=1.0, eps=1e-5, mask=None, rows=None, row_block=16):
+    """Same formula as :func:`triangle_attention`, applied to blocks of pair rows so
+    that large N fits in host memory (rows are independent given the shared bias).
+    ``rows`` optionally restricts the output to a subset of row indices (returned in
+    that order), which is how bounded CPU samples of a large workload are taken."""
+    (X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o) = _f32(
+        X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o)
+    N, _, Cin = X.shape
+    xln = F.layer_norm(X, (Cin,), W_ln, B_ln, eps=eps)
+    bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
+    bp = (xln @ W_proj_z + bz).permute(2, 0, 1).unsqueeze(0)  # (1,H,N,N), shared by every row
+    m = None if mask is None else mask.detach().to("cpu").bool()
+    row_ids = torch.arange(N) if rows is None else torch.as_tensor(rows)
+    outs = []
+    for s in range(0, len(row_ids), row_block):
+        ids = row_ids[s:s + row_block]
+        xr = xln[ids]  # (R, N, C)
+        R = xr.shape[0]
+        q = (xr @ WQ).view(R, N, H, D).permute(0, 2, 1, 3)
+        k = (xr @ WK).view(R, N, H, D).permute(0, 2, 1, 3)
+        v = (xr @ WV).view(R, N, H, D).permute(0, 2, 1, 3)
+        scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
+        if m is not None:
+            scores = scores + torch.where(m[ids][:, None, None, :], 0.0, -1e9)
+        o = torch.matmul(torch.softmax(scores, -1), v).permute(0, 2, 1, 3).reshape(R, N, H * D)
+        g = torch.sigmoid(F.linear(xr, W_proj_g, B_proj_g)).view(R, N, H, D)
+        o = (o.view(R, N, H, D) * g).reshape(R, N, H * D)
+        outs.append(F.linear(o, W_proj_o, B_proj_o))
+    return torch.cat(outs, 0)
+
+
+# --------------------------------------------------------------------------- #
+# triangle multiplicative update (references.py:208-221)
+# --------------------------------------------------------------------------- #
+def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, **w):
+    """(B, L, L, C) -> (B, L, L, C), fp32 CPU.
+
+    g = (LN_in(x) p_in^T) * sigma(LN_in(x) g_in^T) [* mask] (``references.py:210-214``);
+    a, b = chunk(g, 2); outgoing y = einsum(bikd,bjkd->bijd), incoming einsum(bkid,bkjd->bijd);
+    out = (LN_out(y) p_out^T) * sigma(LN_in(x) g_out^T) (``references.py:221``).
+    """
+    if direction not in ("outgoing", "incoming"):
+        raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
+    (x,) = _f32(x)
+    w = {k: _f32(v)[0] for k, v in w.items()}
+    C = x.shape[-1]
+    xln = F.layer_norm(x, (C,), w["norm_in_weight"], w["norm_in_bias"], eps=eps)
+    g = F.linear(xln, w["p_in_weight"]) * F.linear(xln, w["g_in_weight"]).sigmoid()
+    if mask is not None:
+        g = g * mask.detach().to("cpu", torch.float32).unsqueeze(-1)
+    a, b = torch.chunk(g, 2, dim=-1)
+    if direction == "outgoing":
+        y = torch.einsum("bikd,bjkd->bijd", a, b)
+    else:
+        y = torch.einsum("bkid,bkjd->bijd", a, b)
+    yln = F.layer_norm(y, y.shape[-1:], w["norm_out_weight"], w["norm_out_bias"], eps=eps)
+    return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
+
+
+def triangle_multiplicative_update_rows(x, *, direction, rows, mask=None, eps=1e-5, **w):
+    """Output rows ``rows`` (pair-row indices i) of :func:`triangle_multiplicative_update`
+    for batch 0, computed without materialising the full output — used for bounded
+    CPU samples at large L. Same formula as the full function."""
+    (x,) = _f32(x)
+    w = {k: _f32(v)[0] for k, v in w.items()}
+    C = x.shape[-1]
+    xln = F.layer_norm(x[0], (C,), w["norm_in_weight"], w["norm_in_bias"], eps=eps)  # (L,L,C)
+    g = F.linear(xln, w["p_in_weight"]) * F.linear(xln, w["g_in_weight"]).sigmoid()
+    if mask is not None:
+        g = g * mask.detach().to("cpu", torch.float32)[0].unsqueeze(-1)
+    a, b = torch.chunk(g, 2, dim=-1)
+    ids = torch.as_tensor(rows)
+    if direction == "outgoing":
+        y = torch.einsum("ikd,jkd->ijd", a[ids], b)
+    elif direction == "incoming":
+        y = torch.einsum("kid,kjd->ijd", a[:, ids], b)
+    else:
+        raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
+    yln = F.layer_norm(y, y.shape[-1:], w["norm_out_weight"], w["norm_out_bias"], eps=eps)
+    return F.linear(yln, w["p_out_weight"]) * F.linear(xln[ids], w["g_out_weight"]).sigmoid()
+
+
+# --------------------------------------------------------------------------- #
+# attention with pair bias (references.py:143-171, 224-277)
+# --------------------------------------------------------------------------- #
+def attention_pair_bias(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
+                        H, D, scale=1.0, eps=1e-5):
+    """(M, c_s), (M, M, C_z) -> (M, c_s), fp32 CPU. Scale multiplies q, gate on raw X
+    (``references.py:160-171``)."""
+    (X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o) = _f32(
+        X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o)
+    M, N = X.shape
+    Cz = Z.shape[-1]
+    q = (X @ WQ).reshape(M, H, D).permute(1, 0, 2)
+    k = (X @ WK).reshape(M, H, D).permute(1, 0, 2)
+    v = (X @ WV).reshape(M, H, D).permute(1, 0, 2)
+    bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
+    bp = (F.layer_norm(Z, (Cz,), W_ln, B_ln, eps=eps) @ W_proj_z + bz).permute(2, 0, 1)
+    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
+    o = torch.matmul(torch.softmax(scores, -1), v).permute(1, 0, 2).reshape(M, N)
+    g = torch.sigmoid(F.linear(X, W_proj_g, B_proj_g))
+    return F.linear(g * o, W_proj_o, B_proj_o)
+
+
+def attention_pair_bias_masked(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, H, D, *,
+                               key_mask=None, scale=1.0, eps=1e-5, B_proj_g=None, B_proj_o=None):
+    """Key-masked attention with pair bias (``references.py:224-277`` with b_q = 0 and no
+    qk-norm): masked keys get -inf before the softmax (``references.py:273-274``)."""
+    (X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, B_proj_g, B_proj_o) = _f32(
+        X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, B_proj_g, B_proj_o)
+    M, _ = X.shape
+    Cz = Z.shape[-1]
+    q = (X @ WQ).view(M, H, D).permute(1, 0, 2)
+    k = (X @ WK).view(M, H, D).permute(1, 0, 2)
+    v = (X @ WV).view(M, H, D).permute(1, 0, 2)
+    bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
+    bp = (F.layer_norm(Z, (Cz,), W_ln, B_ln, eps=eps) @ W_proj_z + bz).permute(2, 0, 1)
+    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
+    if key_mask is not None:
+        scores = scores.masked_fill(~key_mask.detach().to("cpu").bool().reshape(-1)[None, None, :], float("-inf"))
+    o = torch.matmul(torch.softmax(scores, -1), v).permute(1, 0, 2).reshape(M, H * D)
+    g = torch.sigmoid(F.linear(X, W_proj_g, B_proj_g))
+    return F.linear(g * o, W_proj_o, B_proj_o)

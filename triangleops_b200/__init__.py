@@ -1,2 +1,23 @@
-"""triangleops_b200 — B200-native (sm_100a) TriangleOps."""
+"""triangleops_b200 — B200-native (sm_100a) TriangleOps.
+
+Drop-in for the ``triangle_ops`` Python API (``triangle_ops/__init__.py:17-31``):
+
+    attention_pair_bias            — QKV proj + LN(Z) bias + attention, then gate + W_o
+    triangle_attention             — LN + Q/K/V/bias proj + attention, then gate + W_o
+    triangle_multiplicative_update — LN + gated proj, triangular contraction, LN + gated proj
+
+Each op module exposes ``precompute(...)`` (one-time weight prep -> opaque dict),
+``forward(x, pre, ...)`` (per call) and the one-shot ``<op_name>(...)``.
+All compute runs in hand-written sm_100a kernels behind a C-ABI library
+(``libtriangleops_b200.so``); there is no CPU fallback.
+"""
+
+from . import triangle_attn
+from .triangle_attn import triangle_attention
+
 __version__ = "0.1.0"
+
+__all__ = [
+    "triangle_attn",
+    "triangle_attention",
+]

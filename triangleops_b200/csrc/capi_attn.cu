@@ -1,0 +1,213 @@
+// capi_attn.cu — C-ABI entry points of the attention ops (triangle attention,
+// fused gate, attention with pair bias). Declared in include/triangleops_b200.h.
+#include <cuda_runtime.h>
+#include "sm100.cuh"
+#include "status.h"
+#include "tmap.h"
+
+namespace tops {
+
+inline int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline CUtensorMapDataType tmap_dtype(int dtype) {
+  return dtype == TOPS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? TOPS_OK : TOPS_ERR_CUDA; }
+
+template <typename K>
+inline void set_smem(K kernel, size_t bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+// 2-D row-major [rows][C] operand, 128-row x 64-column boxes, 128B swizzle
+inline bool map_rows(CUtensorMap* m, int dtype, const void* p, int64_t rows, int64_t C, uint32_t box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(C), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(C) * 2};
+  const uint32_t box[2] = {64, box_rows};
+  return make_tmap(m, tmap_dtype(dtype), 2, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// ---------------------------------------------------------------------------
+// projection
+// ---------------------------------------------------------------------------
+template <typename T, int C, int D, bool LN, bool BP>
+int launch_proj(int dtype, const void* x, const void* w, const ProjArgs& args, cudaStream_t st) {
+  using Cfg = ProjCfg<C, BP>;
+  CUtensorMap mx, mw;
+  if (!map_rows(&mx, dtype, x, args.T, C, 128)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mw, dtype, w, Cfg::NOUT, C, Cfg::WBOX)) return TOPS_ERR_TMAP;
+  const size_t smem = sizeof(ProjSmem<C, BP>) + 1024;
+  auto kern = proj_kernel<T, C, D, LN, BP>;
+  set_smem(kern, smem);
+  const int tiles = (args.T + 127) / 128;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, 384, smem, st>>>(mx, mw, args);
+  return launch_status();
+}
+
+template <typename T, int C, int D>
+int dispatch_proj(int dtype, bool ln, bool bp, const void* x, const void* w, const ProjArgs& args, cudaStream_t st) {
+  if (ln && bp) return launch_proj<T, C, D, true, true>(dtype, x, w, args, st);
+  if (!ln && bp) return launch_proj<T, C, D, false, true>(dtype, x, w, args, st);
+  if (!ln && !bp) return launch_proj<T, C, D, false, false>(dtype, x, w, args, st);
+  return launch_proj<T, C, D, true, false>(dtype, x, w, args, st);
+}
+
+int run_proj(int dtype, int C, int D, bool ln, bool bp, const void* x, const void* w, const ProjArgs& args,
+             cudaStream_t st) {
+  if (dtype == TOPS_BF16) {
+    if (C == 128 && D == 32) return dispatch_proj<__nv_bfloat16, 128, 32>(dtype, ln, bp, x, w, args, st);
+    if (C == 64 && D == 16) return dispatch_proj<__nv_bfloat16, 64, 16>(dtype, ln, bp, x, w, args, st);
+  } else if (dtype == TOPS_F16) {
+    if (C == 128 && D == 32) return dispatch_proj<__half, 128, 32>(dtype, ln, bp, x, w, args, st);
+    if (C == 64 && D == 16) return dispatch_proj<__half, 64, 16>(dtype, ln, bp, x, w, args, st);
+  }
+  return TOPS_ERR_SHAPE;
+}
+
+// ---------------------------------------------------------------------------
+// attention
+// ---------------------------------------------------------------------------
+template <typename T, int D, int TR, int TQ>
+int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
+                const void* maskf, const void* bias, void* out, cudaStream_t st) {
+  using Cfg = AttnCfg<D, TR, TQ>;
+  const CUtensorMapDataType dt = tmap_dtype(dtype);
+  const CUtensorMapSwizzle qk_sw = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUtensorMap mq, mk, mv, mm, mb;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nq), static_cast<uint64_t>(R) * H};
+    const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nq) * D * 2};
+    const uint32_t box[3] = {D, 128, 1};
+    if (!make_tmap(&mq, dt, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nk), static_cast<uint64_t>(R) * H};
+    const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nk) * D * 2};
+    const uint32_t box[3] = {D, Cfg::BK, 1};
+    if (!make_tmap(&mk, dt, 3, k, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(D), static_cast<uint64_t>(R) * H};
+    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * D * 2};
+    const uint32_t box[3] = {Cfg::BK, D, 1};
+    if (!make_tmap(&mv, dt, 3, vt, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(R)};
+    const uint64_t str[1] = {static_cast<uint64_t>(Nkp) * 2};
+    const uint32_t box[2] = {Cfg::BK, 1};
+    if (!make_tmap(&mm, dt, 2, maskf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(Nq), static_cast<uint64_t>(H)};
+    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * Nq * 2};
+    const uint32_t box[3] = {Cfg::BK, 128, 1};
+    if (!make_tmap(&mb, dt, 3, bias, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  }
+  AttnArgs args{R, Nq, Nk, out, H};
+  const size_t smem = sizeof(AttnSmem<D, TR, TQ>) + 1024;
+  auto kern = attn_kernel<T, D, TR, TQ>;
+  set_smem(kern, smem);
+  dim3 grid((Nq + 128 * TQ - 1) / (128 * TQ), (R + TR - 1) / TR, H);
+  kern<<<grid, 128 + 128 * Cfg::NWG, smem, st>>>(mq, mk, mv, mm, mb, args);
+  return launch_status();
+}
+
+// TR rows share one bias tile (TR > 1 only pays off when many rows share the bias).
+template <int TR, int TQ>
+int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
+             const void* maskf, const void* bias, void* out, cudaStream_t st) {
+  if (dtype == TOPS_BF16) {
+    if (D == 32) return launch_attn<__nv_bfloat16, 32, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 16) return launch_attn<__nv_bfloat16, 16, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+  } else if (dtype == TOPS_F16) {
+    if (D == 32) return launch_attn<__half, 32, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 16) return launch_attn<__half, 16, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+  }
+  return TOPS_ERR_SHAPE;
+}
+
+// ---------------------------------------------------------------------------
+// gate
+// ---------------------------------------------------------------------------
+template <typename T, int C>
+int launch_gate(int dtype, int64_t T_, const void* o, const void* gin, const void* wg, const void* wo, const float* bg,
+                const float* bo, void* out, cudaStream_t st) {
+  CUtensorMap mg, mo, mwg, mwo;
+  if (!map_rows(&mg, dtype, gin, T_, C, 128)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mo, dtype, o, T_, C, 128)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mwg, dtype, wg, C, C, C)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mwo, dtype, wo, C, C, C)) return TOPS_ERR_TMAP;
+  GateArgs args{static_cast<int>(T_), bg, bo, out};
+  const size_t smem = sizeof(GateSmem<C>) + 1024;
+  auto kern = gate_kernel<T, C>;
+  set_smem(kern, smem);
+  const int tiles = static_cast<int>((T_ + 127) / 128);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, 384, smem, st>>>(mg, mo, mwg, mwo, args);
+  return launch_status();
+}
+
+int run_gate(int dtype, int64_t T_, int64_t C, const void* o, const void* gin, const void* wg, const void* wo,
+             const float* bg, const float* bo, void* out, cudaStream_t st) {
+  if (dtype == TOPS_BF16) {
+    if (C == 128) return launch_gate<__nv_bfloat16, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+    if (C == 64) return launch_gate<__nv_bfloat16, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+  } else if (dtype == TOPS_F16) {
+    if (C == 128) return launch_gate<__half, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+    if (C == 64) return launch_gate<__half, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+  }
+  return TOPS_ERR_SHAPE;
+}
+
+inline bool attn_shape_ok(int64_t C, int64_t H, int64_t D) {
+  return (C == 128 && H == 4 && D == 32) || (C == 64 && H == 4 && D == 16);
+}
+
+}  // namespace tops
+
+using namespace tops;
+
+extern "C" int tops_triangle_attn_forward(int dtype, int64_t N, int64_t C, int64_t H, int64_t D, const void* x,
+                                          int apply_ln, const float* ln_w, const float* ln_b, const void* w_qkvz,
+                                          const float* bz, const uint8_t* mask, float scale, float eps, void* xln_ws,
+                                          void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws,
+                                          void* o_out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (N <= 0 || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
+  if (N * N >= (int64_t(1) << 31)) return TOPS_ERR_SHAPE;
+  if (apply_ln && (ln_w == nullptr || ln_b == nullptr)) return TOPS_ERR_ARG;
+  const void* ptrs[] = {x, w_qkvz, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  if (xln_ws != nullptr && !aligned16(xln_ws)) return TOPS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n = static_cast<int>(N);
+  const int nkp = (n + 7) & ~7;
+  ProjArgs pa{n * n, n, n, nkp, scale, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
+              q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
+  int rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa, st);
+  if (rc != TOPS_OK) return rc;
+  return run_attn<2, 2>(dtype, static_cast<int>(D), n, static_cast<int>(H), n, n, nkp, q_ws, k_ws, vt_ws, maskf_ws,
+                        bias_ws, o_out, st);
+}
+
+extern "C" int tops_fused_gate_forward(int dtype, int64_t T_, int64_t C, const void* o, const void* gin,
+                                       const void* wg, const void* wo, const float* bg, const float* bo, void* out,
+                                       void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (T_ <= 0 || T_ >= (int64_t(1) << 31) || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {o, gin, wg, wo, out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream));
+}

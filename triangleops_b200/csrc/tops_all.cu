@@ -2,3 +2,7 @@
 // C-ABI entry point lives in one translation unit (no relocatable device code).
 #include "common.cu"
 #include "selftest.cu"
+#include "proj.cu"
+#include "attn.cu"
+#include "gate.cu"
+#include "capi_attn.cu"

@@ -1,0 +1,125 @@
+"""Low-level triangle-attention launchers over the C-ABI (replaces the reference's
+Triton ``triangle_ops/triangle_attn/kernel.py``).
+
+``triangle_attn_forward`` keeps the reference signature (``kernel.py:256-374``):
+it takes the pre-normalised x~ = LN(x) and writes the attention output into the
+caller's ``out`` (N, N, H*D). ``fused_gate_forward`` keeps ``kernel.py:438-470``.
+``triangle_attn_fused_forward`` is the path ``module.forward`` uses: LN is fused
+into the projection kernel and x~ is produced as a by-product for the gate.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .. import _lib
+from .._common.layouts import deinterleave_kv, qkv_rows
+
+_P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+_lib.register("tops_triangle_attn_forward",
+              [_I, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P, _P])
+_lib.register("tops_fused_gate_forward", [_I, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P])
+
+
+def _mask_u8(mask, shape):
+    """Reference semantics: the mask is cast to int8 and compared with 0
+    (``triangle_attn/kernel.py:326``, ``:235``)."""
+    if mask is None:
+        return None
+    m = mask.reshape(shape)
+    if m.dtype != torch.bool:
+        m = m.to(torch.int8) != 0
+    return m.to(torch.uint8).contiguous()
+
+
+def _workspaces(N, C, H, D, dtype, device, Bias_buf=None):
+    nkp = (N + 7) // 8 * 8
+    q = torch.empty(N, H, N, D, dtype=dtype, device=device)
+    k = torch.empty(N, H, N, D, dtype=dtype, device=device)
+    vt = torch.empty(N, H, D, nkp, dtype=dtype, device=device)
+    maskf = torch.empty(N, nkp, dtype=dtype, device=device)
+    if Bias_buf is not None and nkp == N and Bias_buf.is_contiguous() and Bias_buf.shape == (H, N, N) \
+            and Bias_buf.dtype == dtype:
+        bias = Bias_buf
+    else:
+        bias = torch.empty(H, N, nkp, dtype=dtype, device=device)
+    return q, k, vt, maskf, bias
+
+
+def triangle_attn_fused_forward(X, w_qkvz, ln_w, ln_b, bz, H, D, *, mask=None, scale=1.0, eps=1e-5, out=None,
+                                xln_out=None):
+    """LN(x) fused into the projection; returns (O (N,N,H*D), x~ (N,N,C))."""
+    _lib.require_cuda(X, w_qkvz)
+    dt = _lib.dtype_code(X.dtype)
+    N, N2, C = X.shape
+    assert N == N2, "X must be (N, N, C)"
+    X = X.contiguous()
+    if out is None:
+        out = torch.empty(N, N, H * D, dtype=X.dtype, device=X.device)
+    if xln_out is None:
+        xln_out = torch.empty(N, N, C, dtype=X.dtype, device=X.device)
+    q, k, vt, maskf, bias = _workspaces(N, C, H, D, X.dtype, X.device)
+    m = _mask_u8(mask, (N, N))
+    _lib.call("tops_triangle_attn_forward", dt, N, C, H, D, X.data_ptr(), 1, ln_w.data_ptr(), ln_b.data_ptr(),
+              w_qkvz.data_ptr(), bz.data_ptr(), _lib.ptr(m), float(scale), float(eps), xln_out.data_ptr(),
+              q.data_ptr(), k.data_ptr(), vt.data_ptr(), maskf.data_ptr(), bias.data_ptr(), out.data_ptr(),
+              _lib.stream_ptr(X.device))
+    return out, xln_out
+
+
+def triangle_attn_forward(X_ln, WQ_c, WKV_c, WZ_c, BZ, out, scale=1.0, mask=None, Bias_buf=None, *, WK_c=None,
+                          WV_c=None):
+    """Attention on a pre-normalised x~ (N, N, C) into ``out`` (N, N, H*D)."""
+    _lib.require_cuda(X_ln, WQ_c, out)
+    N, N2, C = X_ln.shape
+    assert N == N2
+    H = WZ_c.shape[0]
+    D = WQ_c.shape[1] // H
+    assert WKV_c.shape == (C, 2 * H * D)
+    assert out.shape == (N, N, H * D)
+    dt = _lib.dtype_code(X_ln.dtype)
+    if WK_c is None or WV_c is None:
+        WK_c, WV_c = deinterleave_kv(WKV_c, H, D)
+    w = qkv_rows(WQ_c.to(X_ln.dtype), WK_c.to(X_ln.dtype), WV_c.to(X_ln.dtype), WZ_c.to(X_ln.dtype))
+    bz = BZ.float().contiguous()
+    X_ln = X_ln.contiguous()
+    dst = out if out.is_contiguous() else torch.empty(N, N, H * D, dtype=X_ln.dtype, device=X_ln.device)
+    q, k, vt, maskf, bias = _workspaces(N, C, H, D, X_ln.dtype, X_ln.device, Bias_buf)
+    m = _mask_u8(mask, (N, N))
+    _lib.call("tops_triangle_attn_forward", dt, N, C, H, D, X_ln.data_ptr(), 0, None, None, w.data_ptr(),
+              bz.data_ptr(), _lib.ptr(m), float(scale), 1e-5, None, q.data_ptr(), k.data_ptr(), vt.data_ptr(),
+              maskf.data_ptr(), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(X_ln.device))
+    if dst is not out:
+        out.copy_(dst)
+    return out
+
+
+def gate_forward(o, gin, WG, WO, BG=None, BO=None, out=None):
+    """out = (o * sigmoid(gin WG^T + BG)) WO^T + BO over (T, C) token rows."""
+    _lib.require_cuda(o, gin, WG, WO)
+    dt = _lib.dtype_code(gin.dtype)
+    C = gin.shape[-1]
+    T = gin.numel() // C
+    o2 = o.reshape(T, C)
+    if not o2.is_contiguous():
+        o2 = o2.contiguous()
+    g2 = gin.reshape(T, C).contiguous()
+    wg = WG.to(gin.dtype).contiguous()
+    wo = WO.to(gin.dtype).contiguous()
+    assert wg.shape == (C, C) and wo.shape == (C, C), "gate requires square (C, C) weights"
+    bg = None if BG is None else BG.float().contiguous()
+    bo = None if BO is None else BO.float().contiguous()
+    if out is None:
+        out = torch.empty(T, C, dtype=gin.dtype, device=gin.device)
+    _lib.call("tops_fused_gate_forward", dt, T, C, o2.data_ptr(), g2.data_ptr(), wg.data_ptr(), wo.data_ptr(),
+              _lib.ptr(bg), _lib.ptr(bo), out.data_ptr(), _lib.stream_ptr(gin.device))
+    return out
+
+
+def fused_gate_forward(o_attn, qx_ln, WG, WO):
+    """Triangle wrap-up: (o_attn * sigmoid(qx_ln WG^T)) WO^T -> (N1, N2, C)."""
+    N1, N2, H, D = o_attn.shape
+    C = H * D
+    return gate_forward(o_attn.reshape(N1, N2, C), qx_ln, WG, WO).view(N1, N2, C)

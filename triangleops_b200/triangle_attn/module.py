@@ -1,0 +1,86 @@
+"""Public API of triangle attention (``triangle_ops/triangle_attn/module.py``).
+
+Same entry points and argument meaning as the reference: ``precompute`` once,
+``forward`` per call, ``triangle_attention`` one-shot. The per-call path is two
+B200 launches plus the gate: [LN + Q/K/V/bias projection] -> [flash attention]
+-> [gate + W_o]. The mask is a pair-level (N, N) key mask, broadcast over heads
+and queries. Ending-node attention is the caller passing the transposed view
+(``X.transpose(0, 1)``, ``mask.T``) and transposing the result back.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .._common.layouts import interleave_kv, qkv_rows
+from .kernel import gate_forward, triangle_attn_fused_forward
+
+
+def precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D):
+    """One-time layout prep (``module.py:19-50``). WQ/WK/WV are (C, H*D) and
+    W_proj_z (C, H) (matmul convention). Returns an opaque dict for ``forward``."""
+    C = WQ.shape[0]
+    assert WQ.shape == WK.shape == WV.shape == (C, H * D)
+    assert W_proj_z.shape == (C, H)
+    dev = WQ.device
+    BZ = torch.zeros(H, device=dev, dtype=torch.float32) if B_proj_z is None else B_proj_z.float().contiguous()
+    ln_w = torch.ones(C, device=dev, dtype=torch.float32) if W_ln is None else W_ln.float().contiguous()
+    ln_b = torch.zeros(C, device=dev, dtype=torch.float32) if B_ln is None else B_ln.float().contiguous()
+    return {
+        # reference keys
+        "WQ_c": WQ.contiguous(),
+        "WKV_c": interleave_kv(WK, WV, H, D).contiguous(),
+        "WK_c": WK.contiguous() if D == 16 else None,
+        "WV_c": WV.contiguous() if D == 16 else None,
+        "WZ_c": W_proj_z.t().contiguous(),
+        "BZ": BZ,
+        "W_ln": W_ln,
+        "B_ln": B_ln,
+        # B200 kernel operands
+        "W_qkvz": qkv_rows(WQ, WK, WV, W_proj_z.t()),
+        "ln_w32": ln_w,
+        "ln_b32": ln_b,
+        "H": H,
+        "D": D,
+    }
+
+
+def _fix_fully_masked_rows(O, X_ln, WV, mask, H, D):
+    """Rows whose key mask is all False: the reference's additive -1e9 makes every
+    score equal in fp32, i.e. a uniform average of V over all N keys
+    (``triangle_attn/kernel.py:233-238``). The B200 kernel drops masked keys exactly,
+    so such rows are patched here with mean_k V[i, k] = (mean_k x~[i, k]) W_V."""
+    dead = ~mask.reshape(mask.shape[0], -1).to(torch.bool).any(dim=1)
+    if bool(dead.any()):
+        idx = dead.nonzero().flatten()
+        mv = (X_ln[idx].float().mean(dim=1) @ WV.float()).to(O.dtype)  # (n_dead, H*D)
+        O[idx] = mv[:, None, :].expand(-1, O.shape[1], -1)
+    return O
+
+
+def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_proj_o, B_proj_o, pad_to=32):
+    """Per-call forward (``module.py:53-121``). X is (N, N, C); returns (N, N, C).
+    ``pad_to`` is accepted for signature compatibility; the TMA-fed kernels handle
+    any N directly, so nothing is padded."""
+    assert B_proj_g is None and B_proj_o is None, (
+        "fused gate path assumes bias-free linear_g / linear_o (K-Fold LinearNoBias)"
+    )
+    H, D = pre["H"], pre["D"]
+    N = X.shape[0]
+    w = pre["W_qkvz"]
+    if w.dtype != X.dtype:
+        w = w.to(X.dtype)
+    O, X_ln = triangle_attn_fused_forward(X, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, mask=mask,
+                                          scale=scale, eps=eps)
+    if mask is not None:
+        WV = w[2 * H * D:3 * H * D].t()
+        _fix_fully_masked_rows(O, X_ln, WV, mask, H, D)
+    return gate_forward(O, X_ln, W_proj_g, W_proj_o).view(N, N, -1)
+
+
+def triangle_attention(X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o, H, D,
+                       scale=1.0, eps=1e-5, mask=None):
+    """One-shot (precompute included), ``module.py:124-156``."""
+    pre = precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D)
+    return forward(X, pre, mask=mask, scale=scale, eps=eps, W_proj_g=W_proj_g, B_proj_g=B_proj_g,
+                   W_proj_o=W_proj_o, B_proj_o=B_proj_o)
