@@ -56,29 +56,34 @@ def absorb_ln_matmul(weight, w_ln, b_ln):
 # triangle attention (references.py:174-205)
 # --------------------------------------------------------------------------- #
 def triangle_attention(X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
-                       H, D, scale=1.0, eps=1e-5, mask=None):
+                       H, D, scale=1.0, eps=1e-5, mask=None, io_round=None):
     """Starting-node triangle attention on a (N, N, C) pair tensor, fp32 CPU.
 
     LN(x) -> Q/K/V = LN(x) @ W (matmul convention), bias Bp[h,q,k] = LN(x)[q,k] @ W_proj_z + B_proj_z,
     S = (Q*scale) K^T + Bp (+ -1e9 where mask[i,k] is False, ``references.py:200-201``),
     O = softmax(S) V, gate sigma(LN(x) @ W_g^T) (``references.py:203``), then W_o.
+
+    ``io_round`` additionally rounds what the reference stores or casts to the IO
+    dtype: LN(x) (``module.py:73``), scaled Q, K, V (``kernel.py:195,219-220``), the bias
+    (``kernel.py:96``), O (``kernel.py:250``) and the gated product (``kernel.py:434``).
     """
     (X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o) = _f32(
         X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o)
     N, _, Cin = X.shape
-    xln = F.layer_norm(X, (Cin,), W_ln, B_ln, eps=eps)
-    q = (xln @ WQ).view(N, N, H, D).permute(0, 2, 1, 3)
-    k = (xln @ WK).view(N, N, H, D).permute(0, 2, 1, 3)
-    v = (xln @ WV).view(N, N, H, D).permute(0, 2, 1, 3)
+    r = io_round
+    xln = _rt(F.layer_norm(X, (Cin,), W_ln, B_ln, eps=eps), r)
+    q = _rt((xln @ WQ) * scale, r).view(N, N, H, D).permute(0, 2, 1, 3)
+    k = _rt(xln @ WK, r).view(N, N, H, D).permute(0, 2, 1, 3)
+    v = _rt(xln @ WV, r).view(N, N, H, D).permute(0, 2, 1, 3)
     bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
-    bp = (xln @ W_proj_z + bz).permute(2, 0, 1).unsqueeze(0)
-    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
+    bp = _rt(xln @ W_proj_z + bz, r).permute(2, 0, 1).unsqueeze(0)
+    scores = torch.matmul(q, k.transpose(-1, -2)) + bp
     if mask is not None:
         m = mask.detach().to("cpu").bool()
         scores = scores + torch.where(m[:, None, None, :], 0.0, -1e9)
-    o = torch.matmul(torch.softmax(scores, -1), v).permute(0, 2, 1, 3).reshape(N, N, H * D)
+    o = _rt(torch.matmul(torch.softmax(scores, -1), v).permute(0, 2, 1, 3).reshape(N, N, H * D), r)
     g = torch.sigmoid(F.linear(xln, W_proj_g, B_proj_g)).view(N, N, H, D)
-    o = (o.view(N, N, H, D) * g).reshape(N, N, H * D)
+    o = _rt((o.view(N, N, H, D) * g).reshape(N, N, H * D), r)
     return F.linear(o, W_proj_o, B_proj_o)
 
 
@@ -117,8 +122,18 @@ def triangle_attention_chunked(X, W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_
 # --------------------------------------------------------------------------- #
 # triangle multiplicative update (references.py:208-221)
 # --------------------------------------------------------------------------- #
-def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, **w):
+def _rt(t, io):
+    """Round to the IO dtype and back (emulates a store/load in that dtype)."""
+    return t if io is None else t.to(io).float()
+
+
+def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, io_round=None, **w):
     """(B, L, L, C) -> (B, L, L, C), fp32 CPU.
+
+    ``io_round`` (e.g. torch.bfloat16) additionally rounds the two intermediates the
+    reference stores in the IO dtype: the gated projection ``ab``
+    (``triangle_mul/kernel.py:148-162``) and the einsum output ``y`` (cuBLAS output in
+    the IO dtype, ``module.py:71-74``). ``None`` = pure fp32.
 
     g = (LN_in(x) p_in^T) * sigma(LN_in(x) g_in^T) [* mask] (``references.py:210-214``);
     a, b = chunk(g, 2); outgoing y = einsum(bikd,bjkd->bijd), incoming einsum(bkid,bkjd->bijd);
@@ -133,11 +148,13 @@ def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, **w):
     g = F.linear(xln, w["p_in_weight"]) * F.linear(xln, w["g_in_weight"]).sigmoid()
     if mask is not None:
         g = g * mask.detach().to("cpu", torch.float32).unsqueeze(-1)
+    g = _rt(g, io_round)
     a, b = torch.chunk(g, 2, dim=-1)
     if direction == "outgoing":
         y = torch.einsum("bikd,bjkd->bijd", a, b)
     else:
         y = torch.einsum("bkid,bkjd->bijd", a, b)
+    y = _rt(y, io_round)
     yln = F.layer_norm(y, y.shape[-1:], w["norm_out_weight"], w["norm_out_bias"], eps=eps)
     return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
 

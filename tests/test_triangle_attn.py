@@ -41,7 +41,8 @@ def test_matches_oracle(device, dtype, N, masked):
     scale = 1.0 / math.sqrt(32)
     out = tops.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask)
     ref = oracle.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask)
-    assert_parity(out, ref, dtype, f"N={N} masked={masked}")
+    rio = oracle.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask, io_round=dtype)
+    assert_parity(out, ref, dtype, f"N={N} masked={masked}", ref_io=rio)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -51,7 +52,8 @@ def test_general_affine(device, dtype, masked):
     scale = 1.0 / math.sqrt(32)
     out = tops.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask)
     ref = oracle.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask)
-    assert_parity(out, ref, dtype, f"general masked={masked}")
+    rio = oracle.triangle_attention(*args, scale=scale, eps=1e-5, mask=mask, io_round=dtype)
+    assert_parity(out, ref, dtype, f"general masked={masked}", ref_io=rio)
 
 
 @pytest.mark.parametrize("masked", [False, True])

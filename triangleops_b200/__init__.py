@@ -12,12 +12,15 @@ All compute runs in hand-written sm_100a kernels behind a C-ABI library
 (``libtriangleops_b200.so``); there is no CPU fallback.
 """
 
-from . import triangle_attn
+from . import triangle_attn, triangle_mul
 from .triangle_attn import triangle_attention
+from .triangle_mul import triangle_multiplicative_update
 
 __version__ = "0.1.0"
 
 __all__ = [
     "triangle_attn",
+    "triangle_mul",
     "triangle_attention",
+    "triangle_multiplicative_update",
 ]

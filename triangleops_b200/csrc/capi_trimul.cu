@@ -1,0 +1,156 @@
+// capi_trimul.cu — C-ABI entry points of the triangle multiplicative update.
+// Declared in include/triangleops_b200.h.
+#include <cuda_runtime.h>
+#include "sm100.cuh"
+#include "status.h"
+#include "tmap.h"
+
+namespace tops {
+
+template <typename T, int C>
+int launch_trimul_in(int dtype, const void* x, const void* w, const LnGateArgs& args, cudaStream_t st) {
+  CUtensorMap mx, mw;
+  if (!map_rows(&mx, dtype, x, args.M, C, 128)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mw, dtype, w, 4 * C, C, 2 * C > 256 ? 256 : 2 * C)) return TOPS_ERR_TMAP;
+  const size_t smem = sizeof(TmInSmem<C>) + 1024;
+  auto kern = trimul_in_kernel<T, C>;
+  set_smem(kern, smem);
+  const long long tiles = (args.M + 127) / 128;
+  const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
+  kern<<<grid, 384, smem, st>>>(mx, mw, args);
+  return launch_status();
+}
+
+template <typename T, int C>
+int launch_trimul_out(int dtype, const void* y, const void* x, const void* w, const LnGateArgs& args, cudaStream_t st) {
+  CUtensorMap my, mx, mw;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(args.M), static_cast<uint64_t>(C)};
+    const uint64_t str[1] = {static_cast<uint64_t>(args.M) * 2};
+    const uint32_t box[2] = {64, C};
+    if (!make_tmap(&my, tmap_dtype(dtype), 2, y, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  }
+  if (!map_rows(&mx, dtype, x, args.M, C, 128)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mw, dtype, w, 2 * C, C, 2 * C)) return TOPS_ERR_TMAP;
+  const size_t smem = sizeof(TmOutSmem<C>) + 1024;
+  auto kern = trimul_out_kernel<T, C>;
+  set_smem(kern, smem);
+  const long long tiles = (args.M + 127) / 128;
+  const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
+  kern<<<grid, 384, smem, st>>>(my, mx, mw, args);
+  return launch_status();
+}
+
+template <typename T, bool MN>
+int launch_contract(int dtype, int nb, int L, const void* a, const void* b, void* y, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  const uint64_t dims[3] = {static_cast<uint64_t>(L), static_cast<uint64_t>(L), static_cast<uint64_t>(nb)};
+  const uint64_t str[2] = {static_cast<uint64_t>(L) * 2, static_cast<uint64_t>(L) * L * 2};
+  if (!MN) {
+    const uint32_t ba[3] = {kCtBK, kCtBM, 1}, bb[3] = {kCtBK, kCtBN, 1};
+    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, dims, str, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mb, tmap_dtype(dtype), 3, b, dims, str, bb, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  } else {
+    const uint32_t bx[3] = {64, kCtBK, 1};
+    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, dims, str, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mb, tmap_dtype(dtype), 3, b, dims, str, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  }
+  CtArgs args{L, nb, y};
+  const size_t smem = sizeof(CtSmem) + 1024;
+  auto kern = trimul_contract_kernel<T, MN>;
+  set_smem(kern, smem);
+  const long long tiles = static_cast<long long>((L + kCtBM - 1) / kCtBM) * ((L + kCtBN - 1) / kCtBN) * nb;
+  const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
+  kern<<<grid, 256, smem, st>>>(ma, mb, args);
+  return launch_status();
+}
+
+int run_trimul_in(int dtype, int C, const void* x, const void* w, const LnGateArgs& args, cudaStream_t st) {
+  if (dtype == TOPS_BF16) {
+    if (C == 128) return launch_trimul_in<__nv_bfloat16, 128>(dtype, x, w, args, st);
+    if (C == 64) return launch_trimul_in<__nv_bfloat16, 64>(dtype, x, w, args, st);
+  } else if (dtype == TOPS_F16) {
+    if (C == 128) return launch_trimul_in<__half, 128>(dtype, x, w, args, st);
+    if (C == 64) return launch_trimul_in<__half, 64>(dtype, x, w, args, st);
+  }
+  return TOPS_ERR_SHAPE;
+}
+
+int run_trimul_out(int dtype, int C, const void* y, const void* x, const void* w, const LnGateArgs& args,
+                   cudaStream_t st) {
+  if (dtype == TOPS_BF16) {
+    if (C == 128) return launch_trimul_out<__nv_bfloat16, 128>(dtype, y, x, w, args, st);
+    if (C == 64) return launch_trimul_out<__nv_bfloat16, 64>(dtype, y, x, w, args, st);
+  } else if (dtype == TOPS_F16) {
+    if (C == 128) return launch_trimul_out<__half, 128>(dtype, y, x, w, args, st);
+    if (C == 64) return launch_trimul_out<__half, 64>(dtype, y, x, w, args, st);
+  }
+  return TOPS_ERR_SHAPE;
+}
+
+int run_contract(int dtype, int direction, int nb, int L, const void* a, const void* b, void* y, cudaStream_t st) {
+  if (dtype == TOPS_BF16)
+    return direction == 0 ? launch_contract<__nv_bfloat16, false>(dtype, nb, L, a, b, y, st)
+                          : launch_contract<__nv_bfloat16, true>(dtype, nb, L, a, b, y, st);
+  return direction == 0 ? launch_contract<__half, false>(dtype, nb, L, a, b, y, st)
+                        : launch_contract<__half, true>(dtype, nb, L, a, b, y, st);
+}
+
+}  // namespace tops
+
+using namespace tops;
+
+extern "C" int tops_trimul_input_phase(int dtype, int64_t M, int64_t C, const void* x, const uint8_t* mask,
+                                       const void* w_in, const float* sum_in, const float* b_in, float eps,
+                                       void* ab_out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (M <= 0 || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {x, w_in, sum_in, b_in, ab_out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  LnGateArgs args{M, eps, sum_in, b_in, mask, ab_out};
+  return run_trimul_in(dtype, static_cast<int>(C), x, w_in, args, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tops_trimul_contract(int dtype, int direction, int64_t nb, int64_t L, const void* a, const void* b,
+                                    void* y, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (direction != 0 && direction != 1) return TOPS_ERR_ARG;
+  if (nb <= 0 || L <= 0 || nb >= (1 << 30) || L >= (1 << 20)) return TOPS_ERR_SHAPE;
+  if (L % 8 != 0) return TOPS_ERR_ALIGN;
+  const void* ptrs[] = {a, b, y};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(L), a, b, y,
+                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const void* y, const void* x,
+                                        const void* w_out, const float* sum_out, const float* b_out, float eps,
+                                        void* out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (M <= 0 || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  if (M % 8 != 0) return TOPS_ERR_ALIGN;
+  const void* ptrs[] = {y, x, w_out, sum_out, b_out, out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  LnGateArgs args{M, eps, sum_out, b_out, nullptr, out};
+  return run_trimul_out(dtype, static_cast<int>(C), y, x, w_out, args, static_cast<cudaStream_t>(stream));
+}
+
+// The whole op: input phase -> contraction -> output phase on one stream.
+// ab_ws: [2C][B*L*L] workspace, y_ws: [C][B*L*L] workspace.
+extern "C" int tops_trimul_forward(int dtype, int direction, int64_t B, int64_t L, int64_t C, const void* x,
+                                   const uint8_t* mask, const void* w_in, const float* sum_in, const float* b_in,
+                                   const void* w_out, const float* sum_out, const float* b_out, float eps,
+                                   void* ab_ws, void* y_ws, void* out, void* stream) {
+  if (direction != 0 && direction != 1) return TOPS_ERR_ARG;
+  const int64_t M = B * L * L;
+  int rc = tops_trimul_input_phase(dtype, M, C, x, mask, w_in, sum_in, b_in, eps, ab_ws, stream);
+  if (rc != TOPS_OK) return rc;
+  const size_t half = static_cast<size_t>(C) * M * 2;
+  rc = tops_trimul_contract(dtype, direction, C * B, L, ab_ws, static_cast<const uint8_t*>(ab_ws) + half, y_ws,
+                            stream);
+  if (rc != TOPS_OK) return rc;
+  return tops_trimul_output_phase(dtype, M, C, y_ws, x, w_out, sum_out, b_out, eps, out, stream);
+}

@@ -6,3 +6,5 @@
 #include "attn.cu"
 #include "gate.cu"
 #include "capi_attn.cu"
+#include "trimul.cu"
+#include "capi_trimul.cu"

@@ -1,0 +1,544 @@
+// trimul.cu — triangle multiplicative update on tcgen05 (replaces
+// triangle_ops/triangle_mul/kernel.py and the cuBLAS einsum of module.py:70-76).
+//
+//   input phase   ab[k, m] = mask[m] * sigmoid(LN(x)[m] g_in[k]) * (LN(x)[m] p_in[k])   (k < 2C)
+//                 with LN folded into the weights: LN(x) W^T = rstd (x Wc^T - mean sumW) + Bc
+//                 [triangle_mul/kernel.py:35-162 with TRANS=True]
+//   contraction   outgoing y[d,i,j] = sum_k a[d,i,k] b[d,j,k]      (both operands K-major)
+//                 incoming y[d,i,j] = sum_k a[d,k,i] b[d,k,j]      (both operands MN-major)
+//   output phase  out[m, c] = sigmoid(LN_in(x)[m] g_out[c]) * (LN_out(y)[m] p_out[c])
+//                 [triangle_mul/kernel.py:282-326, y read D-major]
+//
+// Every phase is a persistent warp-specialised kernel: w0 TMA producer, w1 MMA
+// issuer, w4-7 LayerNorm statistics (from the staged tile in shared memory),
+// w8-11 epilogue (TMEM -> registers -> global).
+#include "sm100.cuh"
+
+namespace tops {
+
+struct LnGateArgs {
+  long long M;           // tokens
+  float eps;
+  const float* sum_w;    // [NOUT] folded column sums (fp32)
+  const float* b_const;  // [NOUT] folded biases (fp32)
+  const uint8_t* mask;   // [M] int8 multiplier (input phase only; nullptr = none)
+  void* out;
+};
+
+// LayerNorm statistics of a 128 x C row-major (K-major, SW128) staged tile row.
+template <typename T, int C>
+__device__ __forceinline__ void row_stats_kmajor(const uint8_t* tile, int row, float& mean, float& rstd, float eps) {
+  using E = Elem<T>;
+  uint32_t pk[C / 2];
+#pragma unroll
+  for (int ka = 0; ka < C / 64; ++ka)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const uint4 u = *reinterpret_cast<const uint4*>(tile + ka * 16384 + sw128_off(row, ch));
+      const int b = ka * 32 + ch * 4;
+      pk[b] = u.x;
+      pk[b + 1] = u.y;
+      pk[b + 2] = u.z;
+      pk[b + 3] = u.w;
+    }
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < C / 2; ++c) s += E::lo(pk[c]) + E::hi(pk[c]);
+  mean = s * (1.0f / C);
+  float v = 0.f;
+#pragma unroll
+  for (int c = 0; c < C / 2; ++c) {
+    const float d0 = E::lo(pk[c]) - mean, d1 = E::hi(pk[c]) - mean;
+    v = fmaf(d0, d0, fmaf(d1, d1, v));
+  }
+  rstd = rsqrtf(v * (1.0f / C) + eps);
+}
+
+// LayerNorm statistics over the K (= channel) axis of token `tok` of a C x 128
+// MN-major SW128 staged tile (two 64-token halves, each C rows of 128 B).
+template <typename T, int C>
+__device__ __forceinline__ void col_stats_mnmajor(const uint8_t* tile, int tok, float& mean, float& rstd, float eps) {
+  using E = Elem<T>;
+  const uint8_t* base = tile + (tok >> 6) * (C * 128) + (tok & 7) * 2;
+  const uint32_t chunk = (tok & 63) >> 3;
+  float vals[C];
+#pragma unroll
+  for (int d = 0; d < C; ++d) {
+    const uint16_t u = *reinterpret_cast<const uint16_t*>(base + d * 128 + ((chunk ^ (d & 7)) << 4));
+    vals[d] = E::lo(static_cast<uint32_t>(u));
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int d = 0; d < C; ++d) s += vals[d];
+  mean = s * (1.0f / C);
+  float v = 0.f;
+#pragma unroll
+  for (int d = 0; d < C; ++d) {
+    const float dd = vals[d] - mean;
+    v = fmaf(dd, dd, v);
+  }
+  rstd = rsqrtf(v * (1.0f / C) + eps);
+}
+
+// ===========================================================================
+// input phase
+// ===========================================================================
+template <int C>
+struct TmInSmem {
+  static constexpr int NOUT = 4 * C;
+  static constexpr int TILE = (C / 64) * 16384;
+  alignas(1024) uint8_t w[(C / 64) * NOUT * 128];
+  alignas(1024) uint8_t x[2][TILE];
+  float mean[2][128];
+  float rstd[2][128];
+  uint64_t bar_w, x_full[2], x_empty[2], st_ready[2], st_free[2], acc_full, acc_empty;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <typename T, int C>
+__global__ void __launch_bounds__(384, 1)
+    trimul_in_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                     LnGateArgs a) {
+  using E = Elem<T>;
+  using S = TmInSmem<C>;
+  constexpr int NOUT = S::NOUT;  // P rows [0, 2C), G rows [2C, 4C)
+  constexpr int KATOMS = C / 64;
+  constexpr int WBOX = 2 * C > 256 ? 256 : 2 * C;
+  extern __shared__ uint8_t smem_raw[];
+  S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tiles = (a.M + 127) / 128;
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar_w, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.x_full[s], 1);
+      mbar_init(&sm.x_empty[s], 1 + 4);
+      mbar_init(&sm.st_ready[s], 4);
+      mbar_init(&sm.st_free[s], 4);
+    }
+    mbar_init(&sm.acc_full, 1);
+    mbar_init(&sm.acc_empty, 4);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_x);
+      mbar_expect_tx(&sm.bar_w, KATOMS * NOUT * 128);
+      for (int ka = 0; ka < KATOMS; ++ka)
+        for (int r0 = 0; r0 < NOUT; r0 += WBOX)
+          tma_load_2d(sm.w + ka * NOUT * 128 + r0 * 128, &map_w, &sm.bar_w, ka * 64, r0);
+      int it = 0;
+      for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&sm.x_empty[s], ((it >> 1) & 1) ^ 1, abort, 401)) break;
+        mbar_expect_tx(&sm.x_full[s], S::TILE);
+        for (int ka = 0; ka < KATOMS; ++ka)
+          tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.x_full[s], ka * 64, static_cast<int>(tile * 128));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr int NCH = 2 * C > 256 ? 256 : 2 * C;  // MMA N per chunk
+      const uint32_t idesc = make_idesc_f16(128, NCH, E::kFmt, false, false);
+      bool ok = mbar_wait(&sm.bar_w, 0, abort, 402);
+      int it = 0;
+      for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&sm.x_full[s], (it >> 1) & 1, abort, 403)) break;
+        if (!mbar_wait(&sm.acc_empty, (it & 1) ^ 1, abort, 404)) break;
+        tc_fence_after();
+        const uint32_t xa = smem_u32(sm.x[s]), wa = smem_u32(sm.w);
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t woff = (kk >> 2) * (NOUT * 128) + (kk & 3) * 32;
+          const uint64_t ad = make_smem_desc(xa + off, 16, 1024, kSw128);
+#pragma unroll
+          for (int n0 = 0; n0 < NOUT; n0 += NCH)
+            mma_ss(tbase + n0, ad, make_smem_desc(wa + woff + n0 * 128, 16, 1024, kSw128), idesc, kk > 0);
+        }
+        mma_commit(&sm.x_empty[s]);
+        mma_commit(&sm.acc_full);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int row = (warp - 4) * 32 + lane;
+    int it = 0;
+    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      if (!mbar_wait(&sm.x_full[s], (it >> 1) & 1, abort, 405)) break;
+      float mean, rstd;
+      row_stats_kmajor<T, C>(sm.x[s], row, mean, rstd, a.eps);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.x_empty[s]);
+      if (!mbar_wait(&sm.st_free[s], ((it >> 1) & 1) ^ 1, abort, 406)) break;
+      sm.mean[s][row] = mean;
+      sm.rstd[s][row] = rstd;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.st_ready[s]);
+    }
+  } else if (warp >= 8) {
+    const int wq = warp - 8;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    T* out = static_cast<T*>(a.out);
+    int it = 0;
+    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 407)) break;
+      const float mean = sm.mean[s][row], rstd = sm.rstd[s][row];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.st_free[s]);
+      if (!mbar_wait(&sm.acc_full, it & 1, abort, 408)) break;
+      tc_fence_after();
+      const long long m = tile * 128 + row;
+      const bool valid = m < a.M;
+      float mval = 1.0f;
+      if (a.mask != nullptr && valid) mval = static_cast<float>(static_cast<int8_t>(a.mask[m]));
+#pragma unroll 1
+      for (int k0 = 0; k0 < 2 * C; k0 += 32) {
+        uint32_t p[32], g[32];
+        tmem_ld32(lane_addr + k0, p);
+        tmem_ld32(lane_addr + 2 * C + k0, g);
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int k = k0 + e;
+            const float pv = fmaf(rstd, __uint_as_float(p[e]) - mean * __ldg(a.sum_w + k), __ldg(a.b_const + k));
+            const float gv = fmaf(rstd, __uint_as_float(g[e]) - mean * __ldg(a.sum_w + 2 * C + k),
+                                  __ldg(a.b_const + 2 * C + k));
+            out[static_cast<long long>(k) * a.M + m] = E::from_f(sigmoid_fast(gv) * pv * mval);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ===========================================================================
+// contraction (per-channel batched GEMM, 128 x 256 tiles, BK = 64, 4 stages)
+// ===========================================================================
+constexpr int kCtBM = 128, kCtBN = 256, kCtBK = 64, kCtStages = 4;
+
+struct CtSmem {
+  alignas(1024) uint8_t a[kCtStages][kCtBM * kCtBK * 2];
+  alignas(1024) uint8_t b[kCtStages][kCtBN * kCtBK * 2];
+  uint64_t full[kCtStages], empty[kCtStages], acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct CtArgs {
+  int L, nb;
+  void* y;  // [nb][L][L]
+};
+
+template <typename T, bool MN>
+__global__ void __launch_bounds__(256, 1)
+    trimul_contract_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           CtArgs a) {
+  using E = Elem<T>;
+  extern __shared__ uint8_t smem_raw[];
+  CtSmem& sm = *reinterpret_cast<CtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nI = (a.L + kCtBM - 1) / kCtBM, nJ = (a.L + kCtBN - 1) / kCtBN;
+  const long long n_tiles = static_cast<long long>(nI) * nJ * a.nb;
+  const int nk = (a.L + kCtBK - 1) / kCtBK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kCtStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.acc_full[s], 1);
+      mbar_init(&sm.acc_empty[s], 4);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+  auto decode = [&](long long tile, int& bb, int& i0, int& j0) {
+    const int per_b = nI * nJ;
+    bb = static_cast<int>(tile / per_b);
+    const int r = static_cast<int>(tile - static_cast<long long>(bb) * per_b);
+    i0 = (r / nJ) * kCtBM;
+    j0 = (r % nJ) * kCtBN;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_a);
+      tma_prefetch_desc(&map_b);
+      int g = 0;  // global k-block counter (stage ring position)
+      for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        int bb, i0, j0;
+        decode(tile, bb, i0, j0);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % kCtStages;
+          if (!mbar_wait(&sm.empty[s], ((g / kCtStages) & 1) ^ 1, abort, 501)) { ok = false; break; }
+          mbar_expect_tx(&sm.full[s], (kCtBM + kCtBN) * kCtBK * 2);
+          const int k0 = kb * kCtBK;
+          if (!MN) {
+            tma_load_3d(sm.a[s], &map_a, &sm.full[s], k0, i0, bb);
+            tma_load_3d(sm.b[s], &map_b, &sm.full[s], k0, j0, bb);
+          } else {
+            for (int h = 0; h < kCtBM / 64; ++h) tma_load_3d(sm.a[s] + h * 8192, &map_a, &sm.full[s], i0 + h * 64, k0, bb);
+            for (int h = 0; h < kCtBN / 64; ++h) tma_load_3d(sm.b[s] + h * 8192, &map_b, &sm.full[s], j0 + h * 64, k0, bb);
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kCtBM, kCtBN, E::kFmt, MN, MN);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait(&sm.acc_empty[acc], ((it >> 1) & 1) ^ 1, abort, 502)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + acc * 256;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % kCtStages;
+          if (!mbar_wait(&sm.full[s], (g / kCtStages) & 1, abort, 503)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aa = smem_u32(sm.a[s]), ba = smem_u32(sm.b[s]);
+#pragma unroll
+          for (int kk = 0; kk < kCtBK / 16; ++kk) {
+            uint64_t ad, bd;
+            if (!MN) {
+              ad = make_smem_desc(aa + kk * 32, 16, 1024, kSw128);
+              bd = make_smem_desc(ba + kk * 32, 16, 1024, kSw128);
+            } else {
+              ad = make_smem_desc(aa + kk * 2048, 8192, 1024, kSw128);
+              bd = make_smem_desc(ba + kk * 2048, 8192, 1024, kSw128);
+            }
+            mma_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&sm.empty[s]);
+        }
+        if (ok) mma_commit(&sm.acc_full[acc]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int wq = warp - 4;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    int it = 0;
+    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      if (!mbar_wait(&sm.acc_full[acc], (it >> 1) & 1, abort, 504)) break;
+      tc_fence_after();
+      int bb, i0, j0;
+      decode(tile, bb, i0, j0);
+      const int i = i0 + row;
+      T* dst = static_cast<T*>(a.y) + (static_cast<size_t>(bb) * a.L + i) * a.L + j0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kCtBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + acc * 256 + c0, r);
+        if (i < a.L) {
+          uint32_t p[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) p[e] = E::pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+          if (j0 + c0 + 32 <= a.L) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) d4[q] = make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+          } else {
+            for (int e = 0; e < 32; ++e)
+              if (j0 + c0 + e < a.L) dst[c0 + e] = E::from_f(__uint_as_float(r[e]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ===========================================================================
+// output phase
+// ===========================================================================
+template <int C>
+struct TmOutSmem {
+  static constexpr int TILE = (C / 64) * 16384;
+  alignas(1024) uint8_t w[2 * (C / 64) * C * 128];  // p_out rows [0,C), g_out rows [C,2C); per K atom
+  alignas(1024) uint8_t y[2][TILE];                 // MN-major: two 64-token halves x C rows
+  alignas(1024) uint8_t x[2][TILE];                 // K-major
+  float st[2][4][128];                              // mean_y, rstd_y, mean_x, rstd_x
+  uint64_t bar_w, in_full[2], in_empty[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <typename T, int C>
+__global__ void __launch_bounds__(384, 1)
+    trimul_out_kernel(const __grid_constant__ CUtensorMap map_y, const __grid_constant__ CUtensorMap map_x,
+                      const __grid_constant__ CUtensorMap map_w, LnGateArgs a) {
+  using E = Elem<T>;
+  using S = TmOutSmem<C>;
+  constexpr int KATOMS = C / 64;
+  extern __shared__ uint8_t smem_raw[];
+  S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long n_tiles = (a.M + 127) / 128;
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.bar_w, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.in_full[s], 1);
+      mbar_init(&sm.in_empty[s], 1 + 4);
+      mbar_init(&sm.st_ready[s], 4);
+      mbar_init(&sm.st_free[s], 4);
+      mbar_init(&sm.acc_full[s], 1);
+      mbar_init(&sm.acc_empty[s], 4);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_y);
+      tma_prefetch_desc(&map_x);
+      mbar_expect_tx(&sm.bar_w, 2 * KATOMS * C * 128);
+      for (int ka = 0; ka < KATOMS; ++ka) tma_load_2d(sm.w + ka * 2 * C * 128, &map_w, &sm.bar_w, ka * 64, 0);
+      int it = 0;
+      for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&sm.in_empty[s], ((it >> 1) & 1) ^ 1, abort, 601)) break;
+        mbar_expect_tx(&sm.in_full[s], 2 * S::TILE);
+        const int m0 = static_cast<int>(tile * 128);
+        for (int h = 0; h < 2; ++h) tma_load_2d(sm.y[s] + h * C * 128, &map_y, &sm.in_full[s], m0 + h * 64, 0);
+        for (int ka = 0; ka < KATOMS; ++ka) tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.in_full[s], ka * 64, m0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_y = make_idesc_f16(128, C, E::kFmt, true, false);
+      const uint32_t id_x = make_idesc_f16(128, C, E::kFmt, false, false);
+      bool ok = mbar_wait(&sm.bar_w, 0, abort, 602);
+      int it = 0;
+      for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&sm.in_full[s], (it >> 1) & 1, abort, 603)) break;
+        if (!mbar_wait(&sm.acc_empty[s], ((it >> 1) & 1) ^ 1, abort, 604)) break;
+        tc_fence_after();
+        const uint32_t ya = smem_u32(sm.y[s]), xa = smem_u32(sm.x[s]), wa = smem_u32(sm.w);
+        const uint32_t acc = tbase + s * 256;
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk) {
+          const uint32_t woff = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
+          // P = y (MN-major, K = channel d) x p_out^T
+          mma_ss(acc, make_smem_desc(ya + kk * 2048, C * 128, 1024, kSw128),
+                 make_smem_desc(wa + woff, 16, 1024, kSw128), id_y, kk > 0);
+          // G = x (K-major) x g_out^T
+          mma_ss(acc + C, make_smem_desc(xa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
+                 make_smem_desc(wa + woff + C * 128, 16, 1024, kSw128), id_x, kk > 0);
+        }
+        mma_commit(&sm.in_empty[s]);
+        mma_commit(&sm.acc_full[s]);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int row = (warp - 4) * 32 + lane;
+    int it = 0;
+    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      if (!mbar_wait(&sm.in_full[s], (it >> 1) & 1, abort, 605)) break;
+      float my, ry, mx, rx;
+      col_stats_mnmajor<T, C>(sm.y[s], row, my, ry, a.eps);
+      row_stats_kmajor<T, C>(sm.x[s], row, mx, rx, a.eps);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.in_empty[s]);
+      if (!mbar_wait(&sm.st_free[s], ((it >> 1) & 1) ^ 1, abort, 606)) break;
+      sm.st[s][0][row] = my;
+      sm.st[s][1][row] = ry;
+      sm.st[s][2][row] = mx;
+      sm.st[s][3][row] = rx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.st_ready[s]);
+    }
+  } else if (warp >= 8) {
+    const int wq = warp - 8;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    int it = 0;
+    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 607)) break;
+      const float my = sm.st[s][0][row], ry = sm.st[s][1][row], mx = sm.st[s][2][row], rx = sm.st[s][3][row];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.st_free[s]);
+      if (!mbar_wait(&sm.acc_full[s], (it >> 1) & 1, abort, 608)) break;
+      tc_fence_after();
+      const long long m = tile * 128 + row;
+      T* dst = static_cast<T*>(a.out) + m * C;
+#pragma unroll 1
+      for (int c0 = 0; c0 < C; c0 += 32) {
+        uint32_t p[32], g[32];
+        tmem_ld32(lane_addr + s * 256 + c0, p);
+        tmem_ld32(lane_addr + s * 256 + C + c0, g);
+        if (m < a.M) {
+          uint32_t o[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float v[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int c = c0 + 2 * e + h;
+              const float pv = fmaf(ry, __uint_as_float(p[2 * e + h]) - my * __ldg(a.sum_w + c), __ldg(a.b_const + c));
+              const float gv =
+                  fmaf(rx, __uint_as_float(g[2 * e + h]) - mx * __ldg(a.sum_w + C + c), __ldg(a.b_const + C + c));
+              v[h] = sigmoid_fast(gv) * pv;
+            }
+            o[e] = E::pack2(v[0], v[1]);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) d4[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[s]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+}  // namespace tops
