@@ -185,41 +185,42 @@ def triangle_multiplicative_update_rows(x, *, direction, rows, mask=None, eps=1e
 # --------------------------------------------------------------------------- #
 # attention with pair bias (references.py:143-171, 224-277)
 # --------------------------------------------------------------------------- #
-def attention_pair_bias(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
-                        H, D, scale=1.0, eps=1e-5):
-    """(M, c_s), (M, M, C_z) -> (M, c_s), fp32 CPU. Scale multiplies q, gate on raw X
-    (``references.py:160-171``)."""
+def _apb(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o, H, D, scale,
+         eps, key_mask, io_round):
     (X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o) = _f32(
         X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o)
-    M, N = X.shape
+    r = io_round
+    M, _ = X.shape
     Cz = Z.shape[-1]
-    q = (X @ WQ).reshape(M, H, D).permute(1, 0, 2)
-    k = (X @ WK).reshape(M, H, D).permute(1, 0, 2)
-    v = (X @ WV).reshape(M, H, D).permute(1, 0, 2)
+    q = _rt(X @ WQ, r).view(M, H, D).permute(1, 0, 2)
+    k = _rt(X @ WK, r).view(M, H, D).permute(1, 0, 2)
+    v = _rt(X @ WV, r).view(M, H, D).permute(1, 0, 2)
     bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
     bp = (F.layer_norm(Z, (Cz,), W_ln, B_ln, eps=eps) @ W_proj_z + bz).permute(2, 0, 1)
-    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
-    o = torch.matmul(torch.softmax(scores, -1), v).permute(1, 0, 2).reshape(M, N)
-    g = torch.sigmoid(F.linear(X, W_proj_g, B_proj_g))
-    return F.linear(g * o, W_proj_o, B_proj_o)
+    scores = torch.matmul(q, k.transpose(-1, -2)) * scale + bp
+    if key_mask is not None:
+        scores = scores.masked_fill(~key_mask.detach().to("cpu").bool().reshape(-1)[None, None, :], float("-inf"))
+    o = _rt(torch.matmul(torch.softmax(scores, -1), v).permute(1, 0, 2).reshape(M, H * D), r)
+    g = _rt(torch.sigmoid(_rt(F.linear(X, W_proj_g, B_proj_g), r)), r)
+    return F.linear(_rt(g * o, r), W_proj_o, B_proj_o)
+
+
+def attention_pair_bias(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
+                        H, D, scale=1.0, eps=1e-5, io_round=None):
+    """(M, c_s), (M, M, C_z) -> (M, c_s), fp32 CPU (``references.py:143-171``): q, k, v = X W,
+    S = (q k^T) * scale + LN(Z) W_proj_z + B_proj_z, softmax, gate sigmoid(X W_g^T + b_g) on raw X.
+
+    ``io_round`` additionally rounds what the reference stores or casts to the IO dtype:
+    q, k, v (``attn_pair_bias/kernel.py:116-131``), the attention output Og
+    (``kernel.py:197-202``) and the torch gate path of ``module.py:65-66`` (linear output,
+    sigmoid, product). The bias logits stay fp32 as in the reference kernel."""
+    return _apb(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o, H, D,
+                scale, eps, None, io_round)
 
 
 def attention_pair_bias_masked(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, H, D, *,
-                               key_mask=None, scale=1.0, eps=1e-5, B_proj_g=None, B_proj_o=None):
+                               key_mask=None, scale=1.0, eps=1e-5, B_proj_g=None, B_proj_o=None, io_round=None):
     """Key-masked attention with pair bias (``references.py:224-277`` with b_q = 0 and no
     qk-norm): masked keys get -inf before the softmax (``references.py:273-274``)."""
-    (X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, B_proj_g, B_proj_o) = _f32(
-        X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, W_proj_o, B_proj_g, B_proj_o)
-    M, _ = X.shape
-    Cz = Z.shape[-1]
-    q = (X @ WQ).view(M, H, D).permute(1, 0, 2)
-    k = (X @ WK).view(M, H, D).permute(1, 0, 2)
-    v = (X @ WV).view(M, H, D).permute(1, 0, 2)
-    bz = B_proj_z if B_proj_z is not None else torch.zeros(H)
-    bp = (F.layer_norm(Z, (Cz,), W_ln, B_ln, eps=eps) @ W_proj_z + bz).permute(2, 0, 1)
-    scores = torch.matmul(q * scale, k.transpose(-1, -2)) + bp
-    if key_mask is not None:
-        scores = scores.masked_fill(~key_mask.detach().to("cpu").bool().reshape(-1)[None, None, :], float("-inf"))
-    o = torch.matmul(torch.softmax(scores, -1), v).permute(1, 0, 2).reshape(M, H * D)
-    g = torch.sigmoid(F.linear(X, W_proj_g, B_proj_g))
-    return F.linear(g * o, W_proj_o, B_proj_o)
+    return _apb(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o, H, D,
+                scale, eps, key_mask, io_round)

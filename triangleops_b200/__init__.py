@@ -12,13 +12,16 @@ All compute runs in hand-written sm_100a kernels behind a C-ABI library
 (``libtriangleops_b200.so``); there is no CPU fallback.
 """
 
-from . import triangle_attn, triangle_mul
+from . import attn_pair_bias, triangle_attn, triangle_mul
+from .attn_pair_bias import attention_pair_bias
 from .triangle_attn import triangle_attention
 from .triangle_mul import triangle_multiplicative_update
 
 __version__ = "0.1.0"
 
 __all__ = [
+    "attn_pair_bias",
+    "attention_pair_bias",
     "triangle_attn",
     "triangle_mul",
     "triangle_attention",

@@ -24,18 +24,18 @@
 
 namespace tops {
 
-template <int D, int TR, int TQ>
+template <int D, int TR, int TQ, bool BF32 = false>
 struct AttnCfg {
   static constexpr int NT = TR * TQ;            // tiles (128 queries x 1 row) per CTA
   static constexpr int NWG = NT >= 2 ? 2 : 1;   // softmax warpgroups
   static constexpr int TPW = NT / NWG;          // tiles per warpgroup
   static constexpr int BK = 64;                 // keys per block
-  static constexpr int NS = 3;                  // pipeline stages
+  static constexpr int NS = BF32 ? 2 : 3;       // pipeline stages
   static constexpr int NPV = D + 16;            // PV N: D value columns + mask row + zero pad
   static constexpr int Q_BYTES = 128 * D * 2;
   static constexpr int K_BYTES = BK * D * 2;
   static constexpr int V_BYTES = NPV * 128;     // NPV rows x 64 keys (128 B, SW128)
-  static constexpr int B_BYTES = 128 * BK * 2;  // bias tile, SW128
+  static constexpr int B_BYTES = 128 * BK * (BF32 ? 4 : 2);  // bias tile (SW128; fp32: two 32-key boxes)
   static constexpr int STAGE = TR * (K_BYTES + V_BYTES) + TQ * B_BYTES;
   static constexpr int STAGE_TX = TR * (K_BYTES + D * 128 + 128) + TQ * B_BYTES;
   static constexpr uint32_t QK_SW = D == 32 ? kSw64 : kSw32;
@@ -52,9 +52,9 @@ struct AttnArgs {
   int H;
 };
 
-template <int D, int TR, int TQ>
+template <int D, int TR, int TQ, bool BF32>
 struct AttnSmem {
-  using Cfg = AttnCfg<D, TR, TQ>;
+  using Cfg = AttnCfg<D, TR, TQ, BF32>;
   alignas(1024) uint8_t q[Cfg::NT][Cfg::Q_BYTES];
   alignas(1024) uint8_t stage[Cfg::NS][Cfg::STAGE];
   uint64_t bar_q;
@@ -67,15 +67,15 @@ struct AttnSmem {
   int abort;
 };
 
-template <typename T, int D, int TR, int TQ>
-__global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ>::NWG, 1)
+template <typename T, int D, int TR, int TQ, bool BF32>
+__global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NWG, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_m,
                 const __grid_constant__ CUtensorMap map_b, AttnArgs a) {
-  using Cfg = AttnCfg<D, TR, TQ>;
+  using Cfg = AttnCfg<D, TR, TQ, BF32>;
   using E = Elem<T>;
   extern __shared__ uint8_t smem_raw[];
-  auto& sm = *reinterpret_cast<AttnSmem<D, TR, TQ>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto& sm = *reinterpret_cast<AttnSmem<D, TR, TQ, BF32>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.z;
   const int row0 = blockIdx.y * TR;
@@ -135,9 +135,11 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ>::NWG, 1)
           tma_load_3d(kt + Cfg::K_BYTES, &map_v, &sm.kv_full[s], k0, 0, rh);
           tma_load_2d(kt + Cfg::K_BYTES + D * 128, &map_m, &sm.kv_full[s], k0, row0 + r);
         }
-        for (int qb = 0; qb < TQ; ++qb)
-          tma_load_3d(sm.stage[s] + TR * (Cfg::K_BYTES + Cfg::V_BYTES) + qb * Cfg::B_BYTES, &map_b, &sm.kv_full[s],
-                      k0, q0 + qb * 128, h);
+        for (int qb = 0; qb < TQ; ++qb) {
+          uint8_t* bt = sm.stage[s] + TR * (Cfg::K_BYTES + Cfg::V_BYTES) + qb * Cfg::B_BYTES;
+          tma_load_3d(bt, &map_b, &sm.kv_full[s], k0, q0 + qb * 128, h);
+          if (BF32) tma_load_3d(bt + 16384, &map_b, &sm.kv_full[s], k0 + 32, q0 + qb * 128, h);
+        }
       }
     }
   } else if (warp == 1) {
@@ -209,16 +211,32 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ>::NWG, 1)
         const uint8_t* brow = sm.stage[s] + TR * (Cfg::K_BYTES + Cfg::V_BYTES) + qb * Cfg::B_BYTES;
         float x[64];
         float mx = -INFINITY;
+        if (BF32) {
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 bu = *reinterpret_cast<const uint4*>(brow + sw128_off(qrow, ch));
-          const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
+          for (int bx = 0; bx < 2; ++bx)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = ch * 8 + 2 * e;
-            x[c] = (__uint_as_float(sv[c]) + E::lo(b4[e])) * kLog2e;
-            x[c + 1] = (__uint_as_float(sv[c + 1]) + E::hi(b4[e])) * kLog2e;
-            mx = fmaxf(mx, fmaxf(x[c], x[c + 1]));
+            for (int ch = 0; ch < 8; ++ch) {
+              const float4 bf = *reinterpret_cast<const float4*>(brow + bx * 16384 + sw128_off(qrow, ch));
+              const float b4[4] = {bf.x, bf.y, bf.z, bf.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c = bx * 32 + ch * 4 + e;
+                x[c] = (__uint_as_float(sv[c]) + b4[e]) * kLog2e;
+                mx = fmaxf(mx, x[c]);
+              }
+            }
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint4 bu = *reinterpret_cast<const uint4*>(brow + sw128_off(qrow, ch));
+            const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = ch * 8 + 2 * e;
+              x[c] = (__uint_as_float(sv[c]) + E::lo(b4[e])) * kLog2e;
+              x[c + 1] = (__uint_as_float(sv[c + 1]) + E::hi(b4[e])) * kLog2e;
+              mx = fmaxf(mx, fmaxf(x[c], x[c + 1]));
+            }
           }
         }
         float m_use = ms[u];

@@ -1,0 +1,46 @@
+// capi_apb.cu — C-ABI entry point of attention with pair bias.
+// Declared in include/triangleops_b200.h.
+#include <cuda_runtime.h>
+#include "sm100.cuh"
+#include "status.h"
+
+namespace tops {
+
+template <typename T>
+int launch_zbias(const void* z, const ZBiasArgs& args, cudaStream_t st) {
+  const long long groups = (args.n_tok + 3) / 4;  // 4 tokens per warp iteration
+  long long blocks = (groups + 7) / 8;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  zbias_kernel<T, 128, 4><<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const T*>(z), args);
+  return launch_status();
+}
+
+}  // namespace tops
+
+using namespace tops;
+
+extern "C" int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int64_t D, const void* x,
+                                const void* w_qkv, const void* z, const float* wc, const float* sum_w,
+                                const float* b_const, const uint8_t* key_mask, float scale, float eps, void* q_ws,
+                                void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws, void* og_out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (M <= 0 || M >= (1 << 20) || Cz != 128 || H != 4 || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {x, w_qkv, z, wc, sum_w, b_const, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, og_out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int m = static_cast<int>(M);
+  const int mkp = (m + 7) & ~7;
+  ZBiasArgs za{static_cast<long long>(M) * M, m, mkp, eps, wc, sum_w, b_const, static_cast<float*>(bias_ws)};
+  int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(z, za, st) : launch_zbias<__half>(z, za, st);
+  if (rc != TOPS_OK) return rc;
+  // Q/K/V projection of the single sequence (no LN, no bias columns); the key
+  // mask zeroes V rows and feeds the row-sum column of the PV MMA.
+  ProjArgs pa{m, m, 1, mkp, scale, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, maskf_ws,
+              nullptr};
+  rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), false, false, x, w_qkv, pa, st);
+  if (rc != TOPS_OK) return rc;
+  return run_attn<1, 2, true>(dtype, static_cast<int>(D), 1, static_cast<int>(H), m, m, mkp, q_ws, k_ws, vt_ws,
+                              maskf_ws, bias_ws, og_out, st);
+}

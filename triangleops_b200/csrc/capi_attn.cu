@@ -76,10 +76,10 @@ int run_proj(int dtype, int C, int D, bool ln, bool bp, const void* x, const voi
 // ---------------------------------------------------------------------------
 // attention
 // ---------------------------------------------------------------------------
-template <typename T, int D, int TR, int TQ>
+template <typename T, int D, int TR, int TQ, bool BF32>
 int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
                 const void* maskf, const void* bias, void* out, cudaStream_t st) {
-  using Cfg = AttnCfg<D, TR, TQ>;
+  using Cfg = AttnCfg<D, TR, TQ, BF32>;
   const CUtensorMapDataType dt = tmap_dtype(dtype);
   const CUtensorMapSwizzle qk_sw = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   CUtensorMap mq, mk, mv, mm, mb;
@@ -108,14 +108,17 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
     if (!make_tmap(&mm, dt, 2, maskf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
   {
+    const uint64_t eb = BF32 ? 4 : 2;
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(Nq), static_cast<uint64_t>(H)};
-    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * Nq * 2};
-    const uint32_t box[3] = {Cfg::BK, 128, 1};
-    if (!make_tmap(&mb, dt, 3, bias, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * eb, static_cast<uint64_t>(Nkp) * Nq * eb};
+    const uint32_t box[3] = {BF32 ? 32u : static_cast<uint32_t>(Cfg::BK), 128, 1};
+    if (!make_tmap(&mb, BF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : dt, 3, bias, dims, str, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOPS_ERR_TMAP;
   }
   AttnArgs args{R, Nq, Nk, out, H};
-  const size_t smem = sizeof(AttnSmem<D, TR, TQ>) + 1024;
-  auto kern = attn_kernel<T, D, TR, TQ>;
+  const size_t smem = sizeof(AttnSmem<D, TR, TQ, BF32>) + 1024;
+  auto kern = attn_kernel<T, D, TR, TQ, BF32>;
   set_smem(kern, smem);
   dim3 grid((Nq + 128 * TQ - 1) / (128 * TQ), (R + TR - 1) / TR, H);
   kern<<<grid, 128 + 128 * Cfg::NWG, smem, st>>>(mq, mk, mv, mm, mb, args);
@@ -123,15 +126,17 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
 }
 
 // TR rows share one bias tile (TR > 1 only pays off when many rows share the bias).
-template <int TR, int TQ>
+template <int TR, int TQ, bool BF32 = false>
 int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
              const void* maskf, const void* bias, void* out, cudaStream_t st) {
   if (dtype == TOPS_BF16) {
-    if (D == 32) return launch_attn<__nv_bfloat16, 32, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
-    if (D == 16) return launch_attn<__nv_bfloat16, 16, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 32)
+      return launch_attn<__nv_bfloat16, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 16)
+      return launch_attn<__nv_bfloat16, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
   } else if (dtype == TOPS_F16) {
-    if (D == 32) return launch_attn<__half, 32, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
-    if (D == 16) return launch_attn<__half, 16, TR, TQ>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 32) return launch_attn<__half, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 16) return launch_attn<__half, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
   }
   return TOPS_ERR_SHAPE;
 }

@@ -8,3 +8,5 @@
 #include "capi_attn.cu"
 #include "trimul.cu"
 #include "capi_trimul.cu"
+#include "zbias.cu"
+#include "capi_apb.cu"

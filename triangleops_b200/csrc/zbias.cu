@@ -1,0 +1,108 @@
+// zbias.cu — attention-pair-bias logits from the raw pair tensor, z read once for
+// all heads (HBM-bound streaming kernel).
+//
+//   bias[h, q, k] = rstd(z[q,k,:]) * (sum_c z[q,k,c] Wc[h,c] - mean(z[q,k,:]) sumW[h]) + Bc[h]
+//
+// i.e. LN(z) W_proj_z + B_proj_z with the LN affine folded into (Wc, sumW, Bc)
+// [attn_pair_bias/module.py:29-35, attn_pair_bias/kernel.py:149-185]. The reference
+// recomputes this inside the attention loop once per head (z read H times); here
+// eight lanes share one token (16-byte vector loads, 256 contiguous bytes per
+// token), merge their partial statistics with warp-shuffle Welford (Chan's
+// pairwise update for equal counts) and reduce the H dot products in the same
+// shuffle tree. The logits stay fp32, as in the reference.
+#include "sm100.cuh"
+
+namespace tops {
+
+struct ZBiasArgs {
+  long long n_tok;      // M * M
+  int M, Mkp;           // query count, padded key stride of the output rows
+  float eps;
+  const float* wc;      // [H][Cz] fp32
+  const float* sum_w;   // [H]
+  const float* b_const; // [H]
+  float* bias;          // [H][M][Mkp] fp32
+};
+
+template <typename T, int CZ, int H>
+__global__ void __launch_bounds__(256) zbias_kernel(const T* __restrict__ z, ZBiasArgs a) {
+  using E = Elem<T>;
+  static_assert(CZ == 128, "one token = 8 lanes x 16 channels");
+  const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+  // this lane's channels: [sub*8, sub*8+8) and [64+sub*8, 64+sub*8+8)
+  float w[H][16];
+#pragma unroll
+  for (int h = 0; h < H; ++h)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      w[h][e] = a.wc[h * CZ + sub * 8 + e];
+      w[h][8 + e] = a.wc[h * CZ + 64 + sub * 8 + e];
+    }
+  float sw[H], bc[H];
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    sw[h] = a.sum_w[h];
+    bc[h] = a.b_const[h];
+  }
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long wid = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long long base = wid * 4; base < a.n_tok; base += warps * 4) {
+    const long long tok = base + grp;
+    const bool valid = tok < a.n_tok;
+    float v[16];
+    if (valid) {
+      const uint4* src = reinterpret_cast<const uint4*>(z + tok * CZ);
+      const uint4 u0 = __ldcs(src + sub), u1 = __ldcs(src + 8 + sub);
+      const uint32_t p[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[2 * e] = E::lo(p[e]);
+        v[2 * e + 1] = E::hi(p[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = 0.f;
+    }
+    float mean = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) mean += v[e];
+    mean *= (1.0f / 16);
+    float m2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float d = v[e] - mean;
+      m2 = fmaf(d, d, m2);
+    }
+    float dot[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) s = fmaf(v[e], w[h][e], s);
+      dot[h] = s;
+    }
+    float n = 16.f;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, mean, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+      const float d = om - mean;
+      mean += 0.5f * d;
+      m2 += o2 + d * d * (0.5f * n);
+      n *= 2.f;
+#pragma unroll
+      for (int h = 0; h < H; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
+    }
+    const float rstd = rsqrtf(m2 * (1.0f / CZ) + a.eps);
+    if (valid && sub < H) {
+      float bv = 0.f;
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+        if (h == sub) bv = fmaf(rstd, dot[h] - mean * sw[h], bc[h]);
+      const long long q = tok / a.M, k = tok - q * a.M;
+      a.bias[(static_cast<long long>(sub) * a.M + q) * a.Mkp + k] = bv;
+    }
+  }
+}
+
+}  // namespace tops
