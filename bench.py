@@ -1,0 +1,377 @@
+"""Benchmark of the TriangleOps B200 hot path (one JSON line on rank 0).
+
+Workload (BASELINE.json config 1 at the north-star size): starting-node triangle
+attention, N=2048 pair rows, H=4, D=32, C=128, bf16, key mask Bernoulli(0.9),
+LN affine 1+0.1N / 0.1N, weights N(0, 1/fan_in), seed 1 — synthetic inputs.
+A step is one triangle_attention forward over the whole (N, N, C) pair tensor.
+With --gpus P (torchrun) the pair rows are sharded in slabs across P ranks and
+the shared bias is all-gathered over NCCL (strong scaling: total work fixed).
+
+  value        device ms per call (max over ranks), inputs resident in HBM
+  e2e          same call through the public API from pinned host buffers, the
+               H2D copy of the inputs and the D2H copy of the output inside
+  roofline     the attention kernel: algorithmic tensor FLOPs / its event time
+  cpu_baseline the fp32 torch oracle (restatement of the reference's pure-torch
+               path) on the host cores, on a bounded row sample, extrapolated
+  ops          (1 GPU only) the other two ops at their configs (3 and 2)
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port, all host threads) on the same workload and prints its line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_DEF, H, D, C = 2048, 4, 32, 128
+REF_H100_MS = 84.35  # reference README.md:60 (triangle_attention N=2048, H100 PCIe)
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def make_inputs(N, device, seed=1):
+    """Config-1 generator: fp32 draws (on the device generator for speed), cast to bf16."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def rn(*s, sd=1.0):
+        return torch.randn(*s, generator=g, device=device, dtype=torch.float32) * sd
+
+    X = rn(N, N, C).to(torch.bfloat16)
+    mask = torch.rand(N, N, generator=g, device=device) < 0.9
+    W_ln = (1 + 0.1 * rn(C)).to(torch.bfloat16)
+    B_ln = (0.1 * rn(C)).to(torch.bfloat16)
+    Wq, Wk, Wv, Wg, Wo = (rn(C, C, sd=C**-0.5).to(torch.bfloat16) for _ in range(5))
+    Wb = rn(H, C, sd=C**-0.5).to(torch.bfloat16)  # (H, C) as in the config; the API takes (C, H)
+    return dict(X=X, mask=mask, W_ln=W_ln, B_ln=B_ln, WQ=Wq, WK=Wk, WV=Wv, W_proj_z=Wb.t().contiguous(),
+                W_proj_g=Wg, W_proj_o=Wo)
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/tops_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_oracle_ms(inp, N, threads):
+    """fp32 torch oracle on the host: two bounded samples (4 and 20 pair rows, each
+    including the full-N LN + bias that every row shares), extrapolated linearly to
+    all N rows. Returns (ms_per_call, sample description)."""
+    from oracle import oracle
+
+    torch.set_num_threads(threads)
+    cpu = {k: v.detach().cpu() for k, v in inp.items()}
+    args = (cpu["X"], cpu["W_ln"], cpu["B_ln"], cpu["WQ"], cpu["WK"], cpu["WV"], cpu["W_proj_z"], None,
+            cpu["W_proj_g"], None, cpu["W_proj_o"], None, H, D)
+
+    def run(k):
+        t0 = time.perf_counter()
+        oracle.triangle_attention_chunked(*args, scale=1 / math.sqrt(D), mask=cpu["mask"], rows=list(range(k)),
+                                          row_block=k)
+        return time.perf_counter() - t0
+
+    ka, kb = 4, 20
+    ta, tb = run(ka), run(kb)
+    per_row = max((tb - ta) / (kb - ka), 1e-9)
+    shared = max(ta - ka * per_row, 0.0)
+    ms = (shared + N * per_row) * 1e3
+    return ms, (f"oracle.triangle_attention_chunked fp32 on {threads} threads: full-N LN+bias plus {ka} and {kb} "
+                f"of {N} pair rows ({ta:.1f}s, {tb:.1f}s), extrapolated linearly in rows")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    N = args.n
+    threads = os.cpu_count() or 1
+    inp = make_inputs(N, "cpu")
+    vals = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        ms, sample = cpu_oracle_ms(inp, N, threads)
+        if i >= args.warmup:
+            vals.append(ms)
+    v = sorted(vals)[len(vals) // 2]
+    line = {"impl": "reference", "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)", "value": v,
+            "unit": "ms", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": v,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": v / REF_H100_MS, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128, "
+                                                       "mask Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)"},
+            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def time_op(fn, iters=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def other_ops(dev):
+    """Config 3 (triangle_mul incoming L=2048) and config 2 (apb M=1024, masked tail)."""
+    import triangleops_b200 as tops
+
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def rn(*s, sd=1.0):
+        return (torch.randn(*s, generator=g, device=dev) * sd).to(torch.bfloat16)
+
+    L = 2048
+    x = rn(1, L, L, C)
+    v = torch.zeros(L, device=dev)
+    v[:1900] = 1
+    mask = (v[:, None] * v[None, :])[None]
+    w = [1 + 0.1 * rn(C), 0.1 * rn(C), rn(2 * C, C, sd=C**-0.5), rn(2 * C, C, sd=C**-0.5), 1 + 0.1 * rn(C),
+         0.1 * rn(C), rn(C, C, sd=C**-0.5), rn(C, C, sd=C**-0.5)]
+    pre = tops.triangle_mul.precompute(*w)
+    ms = time_op(lambda: tops.triangle_mul.forward(x, pre, direction="incoming", mask=mask))
+    flops = 3.02e12
+    _, sus, _, _ = _peaks()
+    out["triangle_multiplicative_update"] = {"config": "incoming L=2048 C=128 bf16, mask tail 1900", "ms": ms,
+                                             "tflops": flops / ms / 1e9, "frac_of_sustained_bf16": flops / ms / 1e9 / sus}
+    del x, mask
+    g2 = torch.Generator(device=dev).manual_seed(2)
+
+    def rn2(*s, sd=1.0):
+        return (torch.randn(*s, generator=g2, device=dev) * sd)
+
+    M = 1024
+    s_raw = rn2(M, C)
+    X = torch.nn.functional.layer_norm(s_raw, (C,), 1 + 0.1 * rn2(C), 0.1 * rn2(C)).to(torch.bfloat16)
+    Z = rn2(M, M, C).to(torch.bfloat16)
+    W_ln, B_ln = (1 + 0.1 * rn2(C)).to(torch.bfloat16), (0.1 * rn2(C)).to(torch.bfloat16)
+    Wq, Wk, Wv, Wg, Wo = (rn2(C, C, sd=C**-0.5).to(torch.bfloat16) for _ in range(5))
+    Wz = rn2(H, C, sd=C**-0.5).to(torch.bfloat16).t().contiguous()
+    km = torch.ones(M, dtype=torch.bool, device=dev)
+    km[-64:] = False
+    pre = tops.attn_pair_bias.precompute(Wq, Wk, Wv, W_ln, B_ln, Wz, None, H, D)
+    ms = time_op(lambda: tops.attn_pair_bias.forward(X, Z, pre, scale=1.0, W_proj_g=Wg, B_proj_g=None,
+                                                     W_proj_o=Wo, B_proj_o=None, mask=km), iters=50)
+    zbytes = M * M * C * 2
+    hbm = _peaks()[2]
+    out["attention_pair_bias"] = {"config": "M=1024 c_s=C_z=128 bf16, last 64 keys masked", "ms": ms,
+                                  "z_gbs": zbytes / ms / 1e6, "frac_of_hbm": zbytes / ms / 1e6 / hbm}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=N_DEF)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-ops", action="store_true", help="skip the other two ops")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch.distributed as dist
+
+    import triangleops_b200 as tops
+    from triangleops_b200 import dist as tdist
+    from triangleops_b200.triangle_attn import kernel as K
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    N = args.n
+    r0, r1 = tdist.slab(N, rank, world)
+    n = r1 - r0
+
+    inp = make_inputs(N, dev)
+    pre = tops.triangle_attn.precompute(inp["W_ln"], inp["B_ln"], inp["WQ"], inp["WK"], inp["WV"], inp["W_proj_z"],
+                                        None, H, D)
+    X = inp["X"][r0:r1].contiguous()
+    mask = inp["mask"][r0:r1].contiguous()
+    scale = 1 / math.sqrt(D)
+    stream = torch.cuda.current_stream()
+    ev_a0, ev_a1 = [], []
+
+    def step(record=False):
+        ws = K.project_rows(X, pre["W_qkvz"], pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=N, mask_rows=mask,
+                            scale=scale)
+        bias_full = tdist.all_gather_rows(ws["bias"], 1) if world > 1 else ws["bias"]
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        O = K.attend_rows(ws, bias_full, H, D)
+        if record:
+            e1.record(stream)
+            ev_a0.append(e0)
+            ev_a1.append(e1)
+        return K.gate_forward(O, ws["xln"], inp["W_proj_g"], inp["W_proj_o"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a0, ev_a1)) / args.steps
+
+    # end to end through the public API from pinned host buffers
+    X_h = X.cpu().pin_memory()
+    m_h = mask.cpu().pin_memory()
+    out_h = torch.empty(n, N, C, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        Xd = X_h.to(dev, non_blocking=True)
+        md = m_h.to(dev, non_blocking=True)
+        if world > 1:
+            o = tdist.triangle_attention_rows(Xd, pre, N=N, mask_rows=md, scale=scale, W_proj_g=inp["W_proj_g"],
+                                              W_proj_o=inp["W_proj_o"])
+        else:
+            o = tops.triangle_attn.forward(Xd, pre, mask=md, scale=scale, W_proj_g=inp["W_proj_g"], B_proj_g=None,
+                                           W_proj_o=inp["W_proj_o"], B_proj_o=None)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_iters = max(3, min(args.steps, 5))
+    e0.record(stream)
+    for _ in range(e2e_iters):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_iters
+
+    if world > 1:
+        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms, e2e_ms = t.tolist()
+
+    bf16_burst, bf16_sus, hbm, src = _peaks()
+    attn_flops = 4.0 * n * N * N * H * D  # QK^T + PV for this rank's rows
+    achieved = attn_flops / attn_ms / 1e9  # TFLOP/s
+    line = None
+    if rank == 0:
+        ops = other_ops(dev) if (world == 1 and not args.no_ops) else None
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            threads = os.cpu_count() or 1
+            cms, sample = cpu_oracle_ms(inp, N, threads)
+            cpu = {"value": cms, "unit": "ms", "cores": threads, "kind": "port", "sample": sample}
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tpath):
+            try:
+                tj = json.load(open(tpath))
+                traffic = tj.get("attn_kernel_bytes_per_launch_N2048") * (n / N)
+            except Exception:
+                traffic = None
+        line = {
+            "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)",
+            "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": ms / REF_H100_MS if N == 2048 else None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128 bf16, mask "
+                                   "Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)",
+                       "parallelism": f"row-slab x{world}, bias all-gather" if world > 1 else "single GPU",
+                       "l2": "inputs (1 GiB pair tensor) exceed the 126 MB L2; no flush needed",
+                       "vs_baseline_ref": "reference 84.35 ms on H100 PCIe (README.md:60)"},
+            "roofline": {"bound": "tensor", "kernel": "attn_kernel (QK^T + PV on tcgen05)",
+                         "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s", "frac": achieved / bf16_sus,
+                         "peak_kind": f"{src} sustained bf16", "frac_of_burst": achieved / bf16_burst,
+                         "kernel_ms": attn_ms, "traffic": traffic},
+            "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": X_h.numel() * 2 + m_h.numel(),
+                    "d2h_bytes_per_step": out_h.numel() * 2},
+            "gpu_launches": 3 * args.steps,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "op_tflops": 5.09e12 * (N / 2048) ** 3 / ms / 1e9,
+        }
+        if ops is not None:
+            line["ops"] = ops
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,137 @@
+/*
+ * triangleops_b200.h — C ABI of libtriangleops_b200.so, the B200 (sm_100a)
+ * implementation of TriangleOps' three Pairformer primitives.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer (16-byte aligned) unless noted; every
+ *     launch goes on `stream` (a cudaStream_t passed as void*), asynchronously.
+ *   - The library never allocates device memory: intermediates are caller-owned
+ *     workspaces whose shapes are given below (elements of the IO dtype unless
+ *     marked fp32). Np = N rounded up to a multiple of 8.
+ *   - dtype: TOPS_F16 (0) or TOPS_BF16 (1) for the tensor-core paths.
+ *   - Return value: TOPS_OK (0) or a negative status (status.h):
+ *       TOPS_ERR_SHAPE  -1  shape mismatch            (reference: AssertionError)
+ *       TOPS_ERR_DTYPE  -2  unsupported IO dtype      (reference: ValueError, _common/dtype.py:19)
+ *       TOPS_ERR_ARG    -3  bad enum, e.g. direction  (reference: ValueError, triangle_mul/module.py:76)
+ *       TOPS_ERR_ALIGN  -4  misaligned pointer/stride
+ *       TOPS_ERR_TMAP   -5  TMA tensor-map encode failed
+ *       TOPS_ERR_CUDA   -6  CUDA launch error
+ *       TOPS_ERR_TIMEOUT -7 a bounded device-side wait gave up (see tops_device_error)
+ *   - Weights are "K-major rows": a projection y = x W (matmul convention) is passed
+ *     as W^T, i.e. (out, in) row-major, the nn.Linear layout.
+ *
+ * Reference citations are paths inside youngchan2/TriangleOps.
+ */
+#ifndef TRIANGLEOPS_B200_H
+#define TRIANGLEOPS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TOPS_F16 0
+#define TOPS_BF16 1
+#define TOPS_F32 2
+
+/* Library version (100 = 0.1.0; reference triangle_ops/__init__.py:22). */
+int tops_version(void);
+/* Human-readable text of a status code. */
+const char* tops_status_string(int code);
+/* Synchronises `stream`, returns TOPS_ERR_TIMEOUT (and the wait-site id in *site)
+ * if any device-side bounded wait gave up since the last call, then clears it. */
+int tops_device_error(void* stream, int* site);
+
+/* Single-tile check of one tcgen05 operand mode (0..3) against the host:
+ * d (fp32) = A B^T in the layout of that mode. Library self-test. */
+int tops_selftest_umma(int mode, const void* a, const void* b, float* d, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * triangle attention (starting node)
+ * Replaces triangle_attn/kernel.py:256-374 (triangle_attn_forward: bias_proj_kernel
+ * + triangle_attn_kernel) and, with apply_ln=1, the F.layer_norm of
+ * triangle_attn/module.py:73-79.
+ *   x        [N][N][C]          raw x (apply_ln=1) or x~ = LN(x) (apply_ln=0)
+ *   ln_w/b   [C] fp32           LayerNorm affine (apply_ln=1)
+ *   w_qkvz   [3C+16][C]         rows WQ^T | WK^T | WV^T | W_proj_z^T (H rows) | zero
+ *   bz       [H] fp32           bias-projection bias
+ *   mask     [N][N] uint8 or NULL (0 = masked key, per row; broadcast over heads/queries)
+ *   xln_ws   [N*N][C]           receives x~ (apply_ln=1; else may be NULL)
+ *   q_ws,k_ws [N][H][N][D], vt_ws [N][H][D][Np], maskf_ws [N][Np], bias_ws [H][N][Np]
+ *   o_out    [N][N][H*D]        attention output (pre-gate)
+ * Supported (C,H,D): (128,4,32), (64,4,16). Rows whose key mask is all zero
+ * produce non-finite values (the Python layer patches them to the reference's
+ * uniform-softmax result). */
+int tops_triangle_attn_forward(int dtype, int64_t N, int64_t C, int64_t H, int64_t D, const void* x, int apply_ln,
+                               const float* ln_w, const float* ln_b, const void* w_qkvz, const float* bz,
+                               const uint8_t* mask, float scale, float eps, void* xln_ws, void* q_ws, void* k_ws,
+                               void* vt_ws, void* maskf_ws, void* bias_ws, void* o_out, void* stream);
+
+/* The two halves of tops_triangle_attn_forward, for row-slab sharding:
+ * project R pair rows (x [R][N][C], mask [R][N]) -> q/k [R][H][N][D], vt [R][H][D][Np],
+ * maskf [R][Np], bias rows bias_ws [H][R][Np] (bias_proj_kernel, triangle_attn/kernel.py:36-98,
+ * restricted to the rows); then attend R rows against the full shared bias [H][N][Np]
+ * (triangle_attn_kernel, triangle_attn/kernel.py:110-253) into o_out [R][N][H*D]. */
+int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D, const void* x,
+                               int apply_ln, const float* ln_w, const float* ln_b, const void* w_qkvz,
+                               const float* bz, const uint8_t* mask, float scale, float eps, void* xln_ws,
+                               void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws, void* stream);
+int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_t D, const void* q_ws,
+                              const void* k_ws, const void* vt_ws, const void* maskf_ws, const void* bias_ws,
+                              void* o_out, void* stream);
+
+/* out[t] = (o[t] * sigmoid(gin[t] wg^T + bg)) wo^T + bo over T tokens of width C.
+ * Replaces triangle_attn/kernel.py:438-470 (fused_gate_forward; bg = bo = NULL) and
+ * attn_pair_bias/module.py:65-66 (gate on raw X, with biases).
+ *   o, gin, out [T][C]; wg, wo [C][C] (out,in); bg, bo [C] fp32 or NULL. C in {64,128}. */
+int tops_fused_gate_forward(int dtype, int64_t T, int64_t C, const void* o, const void* gin, const void* wg,
+                            const void* wo, const float* bg, const float* bo, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * triangle multiplicative update
+ * Input phase — replaces triangle_mul/kernel.py:235-279 (input_phase):
+ *   ab_out[k][m] = mask[m] * sigmoid(LN(x) g_in^T)[m,k] * (LN(x) p_in^T)[m,k], k < 2C, D-major.
+ *   x [M][C]; mask [M] int8 multiplier or NULL; w_in [4C][C] = p_in_c | g_in_c (LN-folded);
+ *   sum_in, b_in [4C] fp32 (folded column sums / biases); ab_out [2C][M]. C in {64,128}. */
+int tops_trimul_input_phase(int dtype, int64_t M, int64_t C, const void* x, const uint8_t* mask, const void* w_in,
+                            const float* sum_in, const float* b_in, float eps, void* ab_out, void* stream);
+/* Triangular contraction — replaces the torch.einsum of triangle_mul/module.py:70-76.
+ *   direction 0 (outgoing): y[n][i][j] = sum_k a[n][i][k] b[n][j][k]
+ *   direction 1 (incoming): y[n][i][j] = sum_k a[n][k][i] b[n][k][j]
+ *   a, b, y [nb][L][L]; L % 8 == 0. */
+int tops_trimul_contract(int dtype, int direction, int64_t nb, int64_t L, const void* a, const void* b, void* y,
+                         void* stream);
+/* Output phase — replaces triangle_mul/kernel.py:282-326 (output_phase):
+ *   out[m][c] = sigmoid(LN_in(x) g_out^T)[m,c] * (LN_out(y) p_out^T)[m,c]
+ *   y [C][M] (D-major), x [M][C]; w_out [2C][C] = p_out_c | g_out_c; sum_out, b_out [2C] fp32;
+ *   out [M][C]; M % 8 == 0. */
+int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const void* y, const void* x, const void* w_out,
+                             const float* sum_out, const float* b_out, float eps, void* out, void* stream);
+/* The whole op (triangle_mul/module.py:55-88 forward): input phase -> contraction ->
+ * output phase. x [B][L][L][C] (L % 8 == 0), mask [B*L*L] int8 or NULL,
+ * ab_ws [2C][B*L*L], y_ws [C][B*L*L], out [B][L][L][C]. */
+int tops_trimul_forward(int dtype, int direction, int64_t B, int64_t L, int64_t C, const void* x, const uint8_t* mask,
+                        const void* w_in, const float* sum_in, const float* b_in, const void* w_out,
+                        const float* sum_out, const float* b_out, float eps, void* ab_ws, void* y_ws, void* out,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------
+ * attention with pair bias
+ * Replaces attn_pair_bias/kernel.py:205-257 (apb_forward / _apb_kernel): writes the
+ * pre-gate attention output og_out [M][H*D].
+ *   x [M][C]; w_qkv [3C][C] rows WQ^T | WK^T | WV^T; z [M][M][Cz] raw pair tensor;
+ *   wc [H][Cz] fp32, sum_w [H] fp32, b_const [H] fp32 (LN(z) folded into the bias
+ *   projection, attn_pair_bias/module.py:29-35); key_mask [M] uint8 or NULL (extension);
+ *   workspaces q_ws, k_ws [H][M][D], vt_ws [H][D][Mp], maskf_ws [Mp], bias_ws [H][M][Mp] fp32.
+ * Supported: Cz = 128, (C,H,D) in {(128,4,32), (64,4,16)}. */
+int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int64_t D, const void* x,
+                     const void* w_qkv, const void* z, const float* wc, const float* sum_w, const float* b_const,
+                     const uint8_t* key_mask, float scale, float eps, void* q_ws, void* k_ws, void* vt_ws,
+                     void* maskf_ws, void* bias_ws, void* og_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIANGLEOPS_B200_H */

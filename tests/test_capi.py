@@ -1,0 +1,72 @@
+"""Host-only checks of the C-ABI library: it loads, exports every symbol the
+public header declares, and rejects bad arguments before touching the GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from triangleops_b200 import _build, _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "triangleops_b200.h")
+
+
+def _declared():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(tops_\w+)\s*\(", txt, re.M)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("tops_triangle_attn_forward", "tops_fused_gate_forward", "tops_trimul_forward", "tops_apb_forward"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_build.build())
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+
+
+def test_version_and_status_strings():
+    assert _lib.lib().tops_version() == 100
+    assert _lib.status_string(0) == "ok"
+    assert "shape" in _lib.status_string(_lib.ERR_SHAPE)
+
+
+def test_errors_map_to_reference_exceptions():
+    with pytest.raises(AssertionError):
+        _lib.check(_lib.ERR_SHAPE, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_DTYPE, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_ARG, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_TIMEOUT, "x")
+
+
+def test_argument_validation_before_launch():
+    """Bad dtype / direction / shape are rejected on the host (no device needed)."""
+    lib = _lib.lib()
+    f = lib.tops_trimul_contract
+    f.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64] + [ctypes.c_void_p] * 4
+    assert f(5, 0, 1, 8, 16, 16, 16, None) == _lib.ERR_DTYPE
+    assert f(_lib.BF16, 7, 1, 8, 16, 16, 16, None) == _lib.ERR_ARG
+    assert f(_lib.BF16, 0, 1, 10, 16, 16, 16, None) == _lib.ERR_ALIGN
+    assert f(_lib.BF16, 0, 1, 8, 0, 16, 16, None) == _lib.ERR_ALIGN
+    g = lib.tops_fused_gate_forward
+    g.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_int64] + [ctypes.c_void_p] * 8
+    assert g(_lib.BF16, 128, 96, 16, 16, 16, 16, None, None, 16, None) == _lib.ERR_SHAPE
+
+
+def test_no_cpu_fallback():
+    import torch
+    import triangleops_b200 as tops
+    x = torch.zeros(1, 8, 8, 128)
+    w = {k: torch.zeros(s) for k, s in (("norm_in_weight", 128), ("norm_in_bias", 128),
+                                        ("p_in_weight", (256, 128)), ("g_in_weight", (256, 128)),
+                                        ("norm_out_weight", 128), ("norm_out_bias", 128),
+                                        ("p_out_weight", (128, 128)), ("g_out_weight", (128, 128)))}
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        tops.triangle_multiplicative_update(x.bfloat16(), direction="outgoing", **w)

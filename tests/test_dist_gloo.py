@@ -1,0 +1,96 @@
+"""World-size-2 gloo test (CPU) of the row-slab sharding host logic: slab
+partitioning and the all-gather of the shared triangle-attention bias. The
+per-rank kernels are replaced by fp32 torch stand-ins; the result must equal
+the unsharded oracle."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from oracle import oracle
+from triangleops_b200 import dist as tdist
+
+
+class CpuOps:
+    @staticmethod
+    def project(X_rows, pre, mask_rows, N, scale, eps):
+        n, _, C = X_rows.shape
+        H, D = pre["H"], pre["D"]
+        xln = F.layer_norm(X_rows, (C,), pre["W_ln"], pre["B_ln"], eps)
+        heads = lambda W: (xln @ W).view(n, N, H, D).permute(0, 2, 1, 3)  # noqa: E731
+        m = torch.ones(n, N, dtype=torch.bool) if mask_rows is None else mask_rows.bool()
+        bias = (xln @ pre["Wz"] + pre["BZ"]).permute(2, 0, 1).contiguous()  # (H, n, N)
+        return dict(q=heads(pre["WQ"]) * scale, k=heads(pre["WK"]), v=heads(pre["WV"]), m=m, bias=bias, xln=xln)
+
+    @staticmethod
+    def attend(ws, bias_full, pre):
+        s = ws["q"] @ ws["k"].transpose(-1, -2) + bias_full[None]
+        s = s + torch.where(ws["m"][:, None, None, :], 0.0, -1e9)
+        o = torch.softmax(s, -1) @ ws["v"]
+        n, H, N, D = o.shape
+        return o.permute(0, 2, 1, 3).reshape(n, N, H * D)
+
+    @staticmethod
+    def gate(O, ws, Wg, Wo):
+        return F.linear(O * torch.sigmoid(F.linear(ws["xln"], Wg)), Wo)
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(7)
+    N, H, D, C = 12, 2, 8, 16
+    r = lambda *s, sd=1.0: torch.randn(*s, generator=g) * sd  # noqa: E731
+    a = dict(X=r(N, N, C), W_ln=1 + 0.1 * r(C), B_ln=0.1 * r(C), WQ=r(C, H * D, sd=C**-0.5),
+             WK=r(C, H * D, sd=C**-0.5), WV=r(C, H * D, sd=C**-0.5), Wz=r(C, H, sd=C**-0.5), BZ=0.1 * r(H),
+             Wg=r(C, C, sd=C**-0.5), Wo=r(C, C, sd=C**-0.5))
+    mask = torch.rand(N, N, generator=g) > 0.2
+    return N, H, D, a, mask
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N, H, D, a, mask = _inputs()
+        r0, r1 = tdist.slab(N, rank, world)
+        pre = dict(H=H, D=D, W_ln=a["W_ln"], B_ln=a["B_ln"], WQ=a["WQ"], WK=a["WK"], WV=a["WV"], Wz=a["Wz"],
+                   BZ=a["BZ"], W_qkvz=torch.cat([a["WQ"].t(), a["WK"].t(), a["WV"].t()]))
+        out = tdist.triangle_attention_rows(a["X"][r0:r1], pre, N=N, mask_rows=mask[r0:r1], scale=D**-0.5,
+                                            W_proj_g=a["Wg"], W_proj_o=a["Wo"], ops=CpuOps)
+        full = tdist.all_gather_rows(out.contiguous(), 0)
+        if rank == 0:
+            q.put(full)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_slab_partition():
+    assert tdist.slab(2048, 3, 8) == (768, 1024)
+    with pytest.raises(AssertionError):
+        tdist.slab(130, 0, 8)
+
+
+def test_sharded_triangle_attention_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    N, H, D, a, mask = _inputs()
+    ref = oracle.triangle_attention(a["X"], a["W_ln"], a["B_ln"], a["WQ"], a["WK"], a["WV"], a["Wz"], a["BZ"],
+                                    a["Wg"], None, a["Wo"], None, H, D, scale=D**-0.5, mask=mask)
+    assert (full - ref).abs().max().item() < 1e-4

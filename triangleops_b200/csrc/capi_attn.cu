@@ -182,28 +182,49 @@ inline bool attn_shape_ok(int64_t C, int64_t H, int64_t D) {
 
 using namespace tops;
 
+extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
+                                          const void* x, int apply_ln, const float* ln_w, const float* ln_b,
+                                          const void* w_qkvz, const float* bz, const uint8_t* mask, float scale,
+                                          float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws,
+                                          void* maskf_ws, void* bias_ws, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (N <= 0 || R <= 0 || R > N || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
+  if (R * N >= (int64_t(1) << 31)) return TOPS_ERR_SHAPE;
+  if (apply_ln && (ln_w == nullptr || ln_b == nullptr)) return TOPS_ERR_ARG;
+  const void* ptrs[] = {x, w_qkvz, bz, q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  if (xln_ws != nullptr && !aligned16(xln_ws)) return TOPS_ERR_ALIGN;
+  const int n = static_cast<int>(N), r = static_cast<int>(R);
+  const int nkp = (n + 7) & ~7;
+  ProjArgs pa{r * n, n, r, nkp, scale, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
+              q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
+  return run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_t D, const void* q_ws,
+                                         const void* k_ws, const void* vt_ws, const void* maskf_ws,
+                                         const void* bias_ws, void* o_out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (N <= 0 || R <= 0 || R * N >= (int64_t(1) << 31) || H != 4 || (D != 32 && D != 16)) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  const int n = static_cast<int>(N);
+  return run_attn<2, 2>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
+                        q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int tops_triangle_attn_forward(int dtype, int64_t N, int64_t C, int64_t H, int64_t D, const void* x,
                                           int apply_ln, const float* ln_w, const float* ln_b, const void* w_qkvz,
                                           const float* bz, const uint8_t* mask, float scale, float eps, void* xln_ws,
                                           void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws,
                                           void* o_out, void* stream) {
-  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
-  if (N <= 0 || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
-  if (N * N >= (int64_t(1) << 31)) return TOPS_ERR_SHAPE;
-  if (apply_ln && (ln_w == nullptr || ln_b == nullptr)) return TOPS_ERR_ARG;
-  const void* ptrs[] = {x, w_qkvz, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out};
-  for (const void* p : ptrs)
-    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
-  if (xln_ws != nullptr && !aligned16(xln_ws)) return TOPS_ERR_ALIGN;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int n = static_cast<int>(N);
-  const int nkp = (n + 7) & ~7;
-  ProjArgs pa{n * n, n, n, nkp, scale, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
-              q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
-  int rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa, st);
+  int rc = tops_triangle_attn_project(dtype, N, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps,
+                                      xln_ws, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, stream);
   if (rc != TOPS_OK) return rc;
-  return run_attn<2, 2>(dtype, static_cast<int>(D), n, static_cast<int>(H), n, n, nkp, q_ws, k_ws, vt_ws, maskf_ws,
-                        bias_ws, o_out, st);
+  return tops_triangle_attn_attend(dtype, N, N, H, D, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out, stream);
 }
 
 extern "C" int tops_fused_gate_forward(int dtype, int64_t T_, int64_t C, const void* o, const void* gin,

@@ -1,0 +1,80 @@
+"""Multi-GPU row-slab sharding (one process per GPU, torch.distributed over NCCL).
+
+The reference is single-device; these wrappers partition the pair representation
+by pair-row slabs, rank r owning rows [r*N/P, (r+1)*N/P), and use a collective
+only where the algorithm exchanges data:
+
+* triangle attention (starting node): rows are independent given the bias
+  Bp[h, q, k], which every row shares. Each rank projects its slab (its rows of
+  Bp come out of the same GEMM), the Bp slabs are all-gathered, then attention and
+  the gate run on local rows. Per rank the exchange is H*N*N*(P-1)/P elements
+  (29 MB at N=2048, P=8).
+
+The per-rank compute steps are looked up on an ``ops`` object so that the host
+logic (slab partitioning, collective assembly) is testable with gloo on CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def slab(N: int, rank: int, world: int) -> tuple[int, int]:
+    """Row range [r0, r1) of ``rank``; N must divide evenly."""
+    if N % world:
+        raise AssertionError(f"N={N} is not divisible by world size {world}")
+    n = N // world
+    return rank * n, (rank + 1) * n
+
+
+def all_gather_rows(local: torch.Tensor, dim: int, group=None) -> torch.Tensor:
+    """All-gather equal slabs along ``dim`` (rank order) into one tensor."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return local
+    moved = local.movedim(dim, 0).contiguous()
+    out = torch.empty((world * moved.shape[0],) + moved.shape[1:], dtype=moved.dtype, device=moved.device)
+    dist.all_gather_into_tensor(out, moved, group=group)
+    return out.movedim(0, dim).contiguous()
+
+
+class KernelOps:
+    """The sm_100a kernels for one rank's slab."""
+
+    @staticmethod
+    def project(X_rows, pre, mask_rows, N, scale, eps):
+        from .triangle_attn.kernel import project_rows
+
+        w = pre["W_qkvz"] if pre["W_qkvz"].dtype == X_rows.dtype else pre["W_qkvz"].to(X_rows.dtype)
+        return project_rows(X_rows, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], pre["H"], pre["D"], N=N,
+                            mask_rows=mask_rows, scale=scale, eps=eps)
+
+    @staticmethod
+    def attend(ws, bias_full, pre):
+        from .triangle_attn.kernel import attend_rows
+
+        return attend_rows(ws, bias_full, pre["H"], pre["D"])
+
+    @staticmethod
+    def gate(O, ws, W_proj_g, W_proj_o):
+        from .triangle_attn.kernel import gate_forward
+
+        return gate_forward(O, ws["xln"], W_proj_g, W_proj_o).view(O.shape[0], O.shape[1], -1)
+
+
+def triangle_attention_rows(X_rows, pre, *, N, mask_rows=None, scale=1.0, eps=1e-5, W_proj_g, W_proj_o, group=None,
+                            ops=KernelOps):
+    """Starting-node triangle attention of this rank's pair rows X_rows (n, N, C);
+    returns the same rows of the output (n, N, C). Collective: all-gather of the
+    shared bias slabs (H, n, Np) -> (H, N, Np)."""
+    ws = ops.project(X_rows, pre, mask_rows, N, scale, eps)
+    bias_full = all_gather_rows(ws["bias"], 1, group)
+    O = ops.attend(ws, bias_full, pre)
+    if mask_rows is not None:
+        from .triangle_attn.module import _fix_fully_masked_rows
+
+        H, D = pre["H"], pre["D"]
+        w = pre["W_qkvz"]
+        _fix_fully_masked_rows(O, ws["xln"], w[2 * H * D:3 * H * D].t(), mask_rows, H, D)
+    return ops.gate(O, ws, W_proj_g, W_proj_o)

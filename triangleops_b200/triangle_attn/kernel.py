@@ -123,3 +123,44 @@ def fused_gate_forward(o_attn, qx_ln, WG, WO):
     N1, N2, H, D = o_attn.shape
     C = H * D
     return gate_forward(o_attn.reshape(N1, N2, C), qx_ln, WG, WO).view(N1, N2, C)
+
+
+_lib.register("tops_triangle_attn_project",
+              [_I, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P])
+_lib.register("tops_triangle_attn_attend", [_I, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P])
+
+
+def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, scale=1.0, eps=1e-5):
+    """LN + Q/K/V/bias projection of R pair rows X_rows (R, N, C).
+
+    Returns dict(q, k, vt, maskf, bias, xln): bias holds this slab's rows of the
+    shared bias, (H, R, Np); the others are row-local attention operands."""
+    _lib.require_cuda(X_rows)
+    R, N2, C = X_rows.shape
+    assert N2 == N
+    dt = _lib.dtype_code(X_rows.dtype)
+    nkp = (N + 7) // 8 * 8
+    dev, dty = X_rows.device, X_rows.dtype
+    ws = dict(q=torch.empty(R, H, N, D, dtype=dty, device=dev), k=torch.empty(R, H, N, D, dtype=dty, device=dev),
+              vt=torch.empty(R, H, D, nkp, dtype=dty, device=dev), maskf=torch.empty(R, nkp, dtype=dty, device=dev),
+              bias=torch.empty(H, R, nkp, dtype=dty, device=dev), xln=torch.empty(R, N, C, dtype=dty, device=dev))
+    X_rows = X_rows.contiguous()
+    m = _mask_u8(mask_rows, (R, N))
+    _lib.call("tops_triangle_attn_project", dt, R, N, C, H, D, X_rows.data_ptr(), 1, ln_w.data_ptr(),
+              ln_b.data_ptr(), w_qkvz.data_ptr(), bz.data_ptr(), _lib.ptr(m), float(scale), float(eps),
+              ws["xln"].data_ptr(), ws["q"].data_ptr(), ws["k"].data_ptr(), ws["vt"].data_ptr(),
+              ws["maskf"].data_ptr(), ws["bias"].data_ptr(), _lib.stream_ptr(dev))
+    return ws
+
+
+def attend_rows(ws, bias_full, H, D, out=None):
+    """Flash attention of the R projected rows in ``ws`` against the full shared bias
+    (H, N, Np) -> O (R, N, H*D)."""
+    R, _, N, _ = ws["q"].shape
+    dt = _lib.dtype_code(ws["q"].dtype)
+    if out is None:
+        out = torch.empty(R, N, H * D, dtype=ws["q"].dtype, device=ws["q"].device)
+    _lib.call("tops_triangle_attn_attend", dt, R, N, H, D, ws["q"].data_ptr(), ws["k"].data_ptr(),
+              ws["vt"].data_ptr(), ws["maskf"].data_ptr(), bias_full.data_ptr(), out.data_ptr(),
+              _lib.stream_ptr(out.device))
+    return out
