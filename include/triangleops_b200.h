@@ -17,6 +17,7 @@
  *       TOPS_ERR_TMAP   -5  TMA tensor-map encode failed
  *       TOPS_ERR_CUDA   -6  CUDA launch error
  *       TOPS_ERR_TIMEOUT -7 a bounded device-side wait gave up (see tops_device_error)
+ *       TOPS_ERR_CAPACITY -8 size beyond a fixed-capacity entry point
  *   - Weights are "K-major rows": a projection y = x W (matmul convention) is passed
  *     as W^T, i.e. (out, in) row-major, the nn.Linear layout.
  *
@@ -129,6 +130,20 @@ int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int
                      const void* w_qkv, const void* z, const float* wc, const float* sum_w, const float* b_const,
                      const uint8_t* key_mask, float scale, float eps, void* q_ws, void* k_ws, void* vt_ws,
                      void* maskf_ws, void* bias_ws, void* og_out, void* stream);
+
+/* No counterpart in the reference. tops_apb_forward for callers that cannot
+ * allocate device memory (a serving runtime or embedding framework that owns a
+ * fixed device-memory budget and forbids allocation after start-up): same
+ * arguments minus the five workspaces, which live in one library-owned static
+ * device array of about 4.6 MB per GPU, held until process exit. Limits: M <= 512,
+ * C = 128, H = 4, D = 32, Cz = 128; M > 512 returns TOPS_ERR_CAPACITY. The array
+ * is shared by all calls on a device — calls that overlap on the GPU race. The
+ * first call on a device looks up the array's address; make it before any stream
+ * capture. */
+int tops_apb_forward_noalloc(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int64_t D, const void* x,
+                             const void* w_qkv, const void* z, const float* wc, const float* sum_w,
+                             const float* b_const, const uint8_t* key_mask, float scale, float eps, void* og_out,
+                             void* stream);
 
 #ifdef __cplusplus
 }

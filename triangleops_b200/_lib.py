@@ -28,6 +28,7 @@ ERR_ALIGN = -4
 ERR_TMAP = -5
 ERR_CUDA = -6
 ERR_TIMEOUT = -7
+ERR_CAPACITY = -8
 
 F16, BF16, F32 = 0, 1, 2
 _DTYPE_CODE = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}

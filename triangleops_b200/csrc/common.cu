@@ -15,6 +15,7 @@ extern "C" const char* tops_status_string(int code) {
     case TOPS_ERR_TMAP: return "TMA tensor-map encode failed";
     case TOPS_ERR_CUDA: return "CUDA error";
     case TOPS_ERR_TIMEOUT: return "device-side wait timed out";
+    case TOPS_ERR_CAPACITY: return "size exceeds the fixed scratch capacity of this entry point";
     default: return "unknown status";
   }
 }

@@ -9,6 +9,7 @@
 #define TOPS_ERR_TMAP (-5)     /* tensor-map encode failed   -> RuntimeError                      */
 #define TOPS_ERR_CUDA (-6)     /* CUDA launch / runtime error -> RuntimeError                     */
 #define TOPS_ERR_TIMEOUT (-7)  /* a device-side bounded wait gave up -> RuntimeError              */
+#define TOPS_ERR_CAPACITY (-8) /* problem larger than a fixed-capacity entry point accepts         */
 
 /* IO dtype enum shared with the Python layer */
 #define TOPS_F16 0

@@ -10,3 +10,4 @@
 #include "capi_trimul.cu"
 #include "zbias.cu"
 #include "capi_apb.cu"
+#include "noalloc.cu"
