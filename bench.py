@@ -79,7 +79,7 @@ class Clocks:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -221,8 +221,8 @@ def other_ops(dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=N_DEF)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -276,11 +276,12 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    clocks = Clocks(local)
+    clocks.start()  # sampling covers warm-up and the timed steps (the timed region alone can be < 1 s)
+    time.sleep(1.0)
     for _ in range(args.warmup):
         step()
     barrier()
-    clocks = Clocks(local)
-    clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
