@@ -99,12 +99,22 @@ class Clocks:
                 rows.append(f)
         if not rows:
             return None
-        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        pw = [num(r[3]) for r in rows]
+        peak_pw = max([p for p in pw if p is not None] or [0.0])
+        # samples under load: power above half of the peak seen (drops the idle lead-in)
+        load = [r for r, p in zip(rows, pw) if p is not None and p >= 0.5 * peak_pw] or rows
+        sm = sorted(num(r[1]) for r in load if num(r[1]) is not None)
         mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        reasons = sorted({n for r in load for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "samples_under_load": len(load), "power_w_max": peak_pw}
 
 
 def cpu_oracle_ms(inp, N, threads):
