@@ -2,7 +2,7 @@
 // (starting node, rows of the pair tensor) and attention-with-pair-bias (one row).
 //
 // Semantics per (row r, head h, query q)  [triangle_attn/kernel.py:194-253]:
-//   S[q,k] = Q[r,h,q,:] . K[r,h,k,:] + bias[h,q,k]          (Q already scaled)
+//   S[q,k] = Q[r,h,q,:] . K[r,h,k,:] + bias[h,q,k]          (Q already scaled; log2 units)
 //   O[r,q,h*D:(h+1)*D] = sum_k softmax_k(S over unmasked k) V[r,h,k,:]
 // The bias is shared by every row r (triangle attention) — one CTA therefore
 // processes TR rows x TQ query blocks for the same head, so each bias tile read
@@ -14,12 +14,22 @@
 // column D. Masked keys therefore contribute to neither O nor l (the reference's
 // -1e9 additive mask gives the same result for any row with >= 1 unmasked key).
 //
-// Per CTA (384 threads): w0 TMA producer, w1 MMA issuer, w4-7 / w8-11 softmax
-// warpgroups (one TMEM lane = one query row per thread). TMEM: per tile an S/P
+// Per CTA: w0 TMA producer, w1 MMA issuer, one softmax warpgroup per tile
+// (one TMEM lane = one query row per thread). TMEM: per tile an S/P
 // region of 64 fp32 columns (P is written back over S as packed 16-bit pairs and
 // fed to the PV MMA straight from TMEM) and an O region of D+16 columns.
-// Online softmax in the exp2 domain with lazy rescaling (O is only rescaled when
-// the running max grows by more than 2^8).
+// Online softmax in the exp2 domain (Q carries scale*log2(e) and the bias log2(e),
+// both folded in by the projection stage) with lazy rescaling (O is only rescaled
+// when the running max grows by more than 2^8). The per-element work runs on f16
+// pairs: S + bias is rounded to f16 (relative error 2^-11, well below the 2^-8
+// rounding the 16-bit Q and K already put into S), the row max is a pairwise tree,
+// and P = ex2.approx.f16x2(x - m) is written back to TMEM as the f16 A operand of
+// the PV MMA; V^T and the mask row are f16 for that MMA.
+//
+// Cost model (measured on B200): one tcgen05.mma with M=128, K=16 occupies the
+// tensor core for about 150 cycles whatever N is up to N=128, so at D=32 this
+// kernel is bound by the number of MMA instructions (QK^T: D/16 per key block,
+// PV: BK/16 per key block), not by FLOPs or by the exponentials.
 #include "sm100.cuh"
 
 namespace tops {
@@ -27,7 +37,7 @@ namespace tops {
 template <int D, int TR, int TQ, bool BF32 = false>
 struct AttnCfg {
   static constexpr int NT = TR * TQ;            // tiles (128 queries x 1 row) per CTA
-  static constexpr int NWG = NT >= 2 ? 2 : 1;   // softmax warpgroups
+  static constexpr int NWG = NT;                // softmax warpgroups (one tile each)
   static constexpr int TPW = NT / NWG;          // tiles per warpgroup
   static constexpr int BK = 64;                 // keys per block
   static constexpr int NS = BF32 ? 2 : 3;       // pipeline stages
@@ -146,7 +156,8 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NWG, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t idesc_qk = make_idesc_f16(128, Cfg::BK, E::kFmt, false, false);
-      const uint32_t idesc_pv = make_idesc_f16(128, Cfg::NPV, E::kFmt, false, false);
+      // P (ex2 output) and V^T are f16 whatever the IO dtype.
+      const uint32_t idesc_pv = make_idesc_f16(128, Cfg::NPV, 0, false, false);
       bool ok = mbar_wait(&sm.bar_q, 0, abort, 202);
       auto issue_pv = [&](int t, int j) {
         const uint8_t* vt = sm.stage[j % Cfg::NS] + (t / TQ) * (Cfg::K_BYTES + Cfg::V_BYTES) + Cfg::K_BYTES;
@@ -193,7 +204,6 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NWG, 1)
     const int wq = warp & 3;
     const int qrow = wq * 32 + lane;  // TMEM lane == query row within the tile
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    constexpr float kLog2e = 1.4426950408889634f;
     float ms[Cfg::TPW];
 #pragma unroll
     for (int u = 0; u < Cfg::TPW; ++u) ms[u] = 0.f;
@@ -206,39 +216,47 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NWG, 1)
         const int qb = t % TQ;
         if (!mbar_wait(&sm.s_full[t], j & 1, abort, 206)) { ok = false; break; }
         tc_fence_after();
-        uint32_t sv[64];
-        tmem_ld64(lane_addr + Cfg::S_COL + t * 64, sv);
         const uint8_t* brow = sm.stage[s] + TR * (Cfg::K_BYTES + Cfg::V_BYTES) + qb * Cfg::B_BYTES;
-        float x[64];
-        float mx = -INFINITY;
-        if (BF32) {
+        // x = S + bias (log2 units), packed to f16 pairs: the rest of the softmax runs
+        // two lanes per instruction. S is read in two 32-column halves.
+        __half2 xh[32];
 #pragma unroll
-          for (int bx = 0; bx < 2; ++bx)
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[32];
+          tmem_ld32(lane_addr + Cfg::S_COL + t * 64 + half * 32, sv);
+          if (BF32) {
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch) {
-              const float4 bf = *reinterpret_cast<const float4*>(brow + bx * 16384 + sw128_off(qrow, ch));
-              const float b4[4] = {bf.x, bf.y, bf.z, bf.w};
+              const float4 bf = *reinterpret_cast<const float4*>(brow + half * 16384 + sw128_off(qrow, ch));
+              xh[half * 16 + ch * 2] = __floats2half2_rn(__uint_as_float(sv[ch * 4]) + bf.x,
+                                                          __uint_as_float(sv[ch * 4 + 1]) + bf.y);
+              xh[half * 16 + ch * 2 + 1] = __floats2half2_rn(__uint_as_float(sv[ch * 4 + 2]) + bf.z,
+                                                              __uint_as_float(sv[ch * 4 + 3]) + bf.w);
+            }
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const int ch = half * 4 + cc;
+              const uint4 bu = *reinterpret_cast<const uint4*>(brow + sw128_off(qrow, ch));
+              const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const int c = bx * 32 + ch * 4 + e;
-                x[c] = (__uint_as_float(sv[c]) + b4[e]) * kLog2e;
-                mx = fmaxf(mx, x[c]);
+                const int c = cc * 8 + 2 * e;
+                xh[half * 16 + cc * 4 + e] =
+                    __hadd2(__floats2half2_rn(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
+                            *reinterpret_cast<const __half2*>(&b4[e]));
               }
-            }
-        } else {
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const uint4 bu = *reinterpret_cast<const uint4*>(brow + sw128_off(qrow, ch));
-            const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = ch * 8 + 2 * e;
-              x[c] = (__uint_as_float(sv[c]) + E::lo(b4[e])) * kLog2e;
-              x[c + 1] = (__uint_as_float(sv[c + 1]) + E::hi(b4[e])) * kLog2e;
-              mx = fmaxf(mx, fmaxf(x[c], x[c + 1]));
             }
           }
         }
+        __half2 mt[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) mt[c] = __hmax2(xh[2 * c], xh[2 * c + 1]);
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int c = 0; c < w; ++c) mt[c] = __hmax2(mt[c], mt[c + w]);
+        const float mx = fmaxf(__low2float(mt[0]), __high2float(mt[0]));
         float m_use = ms[u];
         if (j == 0) {
           m_use = mx;
@@ -266,9 +284,13 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NWG, 1)
           }
         }
         ms[u] = m_use;
+        const __half2 mh = __float2half2_rn(m_use);  // exact: m_use is an f16 value
         uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = E::pack2(ex2_approx(x[2 * c] - m_use), ex2_approx(x[2 * c + 1] - m_use));
+        for (int c = 0; c < 32; ++c) {
+          const __half2 p = h2exp2(__hsub2(xh[c], mh));
+          pk[c] = *reinterpret_cast<const uint32_t*>(&p);
+        }
         tmem_st32(lane_addr + Cfg::S_COL + t * 64, pk);
         tmem_wait_st();
         tc_fence_before();

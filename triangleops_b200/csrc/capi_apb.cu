@@ -37,7 +37,7 @@ extern "C" int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int
   if (rc != TOPS_OK) return rc;
   // Q/K/V projection of the single sequence (no LN, no bias columns); the key
   // mask zeroes V rows and feeds the row-sum column of the PV MMA.
-  ProjArgs pa{m, m, 1, mkp, scale, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, maskf_ws,
+  ProjArgs pa{m, m, 1, mkp, scale * kLog2e, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, maskf_ws,
               nullptr};
   rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), false, false, x, w_qkv, pa, st);
   if (rc != TOPS_OK) return rc;

@@ -14,6 +14,8 @@ inline int sm_count() {
   return n > 0 ? n : 148;
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline CUtensorMapDataType tmap_dtype(int dtype) {
@@ -99,20 +101,22 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(D), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * D * 2};
     const uint32_t box[3] = {Cfg::BK, D, 1};
-    if (!make_tmap(&mv, dt, 3, vt, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vt, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOPS_ERR_TMAP;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(R)};
     const uint64_t str[1] = {static_cast<uint64_t>(Nkp) * 2};
     const uint32_t box[2] = {Cfg::BK, 1};
-    if (!make_tmap(&mm, dt, 2, maskf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, maskf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOPS_ERR_TMAP;
   }
   {
     const uint64_t eb = BF32 ? 4 : 2;
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(Nq), static_cast<uint64_t>(H)};
     const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * eb, static_cast<uint64_t>(Nkp) * Nq * eb};
     const uint32_t box[3] = {BF32 ? 32u : static_cast<uint32_t>(Cfg::BK), 128, 1};
-    if (!make_tmap(&mb, BF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : dt, 3, bias, dims, str, box,
+    if (!make_tmap(&mb, BF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, bias, dims, str, box,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return TOPS_ERR_TMAP;
   }
@@ -197,7 +201,7 @@ extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64
   if (xln_ws != nullptr && !aligned16(xln_ws)) return TOPS_ERR_ALIGN;
   const int n = static_cast<int>(N), r = static_cast<int>(R);
   const int nkp = (n + 7) & ~7;
-  ProjArgs pa{r * n, n, r, nkp, scale, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
+  ProjArgs pa{r * n, n, r, nkp, scale * kLog2e, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
               q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
   return run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa,
                   static_cast<cudaStream_t>(stream));

@@ -6,10 +6,11 @@
 //   x~  = LN(x) (optional; eps, affine w/b; rounded to the IO dtype and also
 //         written out for the gate stage)                [triangle_attn/module.py:73-79]
 //   Q   = (x~ WQ) * scale   -> Q [R][H][Nk][D]           [triangle_attn/kernel.py:194-195]
+//                              (callers pass scale * log2(e): the attention works in log2 units)
 //   K   =  x~ WK            -> K [R][H][Nk][D]
-//   V   = (x~ WV) * m[i,k]  -> Vt[R][H][D][Nkp]  (transposed, masked keys zeroed)
-//   m   = mask[i,k] ? 1 : 0 -> maskf[R][Nkp]     (the PV MMA turns it into the row sum)
-//   Bp  =  x~ WZ^T + BZ     -> Bp[H][R][Nkp]     (optional)  [triangle_attn/kernel.py:36-98]
+//   V   = (x~ WV) * m[i,k]  -> Vt[R][H][D][Nkp]  f16 (transposed, masked keys zeroed)
+//   m   = mask[i,k] ? 1 : 0 -> maskf[R][Nkp]     f16 (the PV MMA turns it into the row sum)
+//   Bp  = (x~ WZ^T + BZ) * log2(e) -> Bp[H][R][Nkp] f16 (optional) [triangle_attn/kernel.py:36-98]
 //
 // One GEMM per 128-token tile: x~ (128 x C, K-major, SW128) times the resident
 // concatenated weight Wcat (NOUT x C, K-major, SW128) into a TMEM accumulator of
@@ -248,9 +249,9 @@ __global__ void __launch_bounds__(384, 1)
         // V (transposed, masked keys zeroed)
         if (D == 32) tmem_ld32(lane_addr + 2 * C + h * D, r); else tmem_ld16(lane_addr + 2 * C + h * D, r);
         if (valid) {
-          T* dst = static_cast<T*>(a.vt) + (static_cast<size_t>(ri) * H + h) * D * a.Nkp + kpos;
+          __half* dst = static_cast<__half*>(a.vt) + (static_cast<size_t>(ri) * H + h) * D * a.Nkp + kpos;
 #pragma unroll
-          for (int d = 0; d < D; ++d) dst[static_cast<size_t>(d) * a.Nkp] = E::from_f(__uint_as_float(r[d]) * mval);
+          for (int d = 0; d < D; ++d) dst[static_cast<size_t>(d) * a.Nkp] = __float2half_rn(__uint_as_float(r[d]) * mval);
         }
       }
       if (HAS_BP) {
@@ -258,10 +259,10 @@ __global__ void __launch_bounds__(384, 1)
         if (valid)
 #pragma unroll
           for (int h = 0; h < H; ++h)
-            static_cast<T*>(a.bp)[(static_cast<size_t>(h) * a.R + ri) * a.Nkp + kpos] =
-                E::from_f(__uint_as_float(r[h]) + bz[h]);
+            static_cast<__half*>(a.bp)[(static_cast<size_t>(h) * a.R + ri) * a.Nkp + kpos] =
+                __float2half_rn((__uint_as_float(r[h]) + bz[h]) * 1.4426950408889634f);
       }
-      if (valid) static_cast<T*>(a.maskf)[static_cast<size_t>(ri) * a.Nkp + kpos] = E::from_f(mval);
+      if (valid) static_cast<__half*>(a.maskf)[static_cast<size_t>(ri) * a.Nkp + kpos] = __float2half_rn(mval);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.bar_acc_empty);

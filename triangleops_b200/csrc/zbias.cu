@@ -21,7 +21,7 @@ struct ZBiasArgs {
   const float* wc;      // [H][Cz] fp32
   const float* sum_w;   // [H]
   const float* b_const; // [H]
-  float* bias;          // [H][M][Mkp] fp32
+  float* bias;          // [H][M][Mkp] fp32, in log2 units (times log2(e))
 };
 
 template <typename T, int CZ, int H>
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256) zbias_kernel(const T* __restrict__ z, ZBi
       for (int h = 0; h < H; ++h)
         if (h == sub) bv = fmaf(rstd, dot[h] - mean * sw[h], bc[h]);
       const long long q = tok / a.M, k = tok - q * a.M;
-      a.bias[(static_cast<long long>(sub) * a.M + q) * a.Mkp + k] = bv;
+      a.bias[(static_cast<long long>(sub) * a.M + q) * a.Mkp + k] = bv * 1.4426950408889634f;  // log2 units
     }
   }
 }

@@ -38,13 +38,14 @@ def _workspaces(N, C, H, D, dtype, device, Bias_buf=None):
     nkp = (N + 7) // 8 * 8
     q = torch.empty(N, H, N, D, dtype=dtype, device=device)
     k = torch.empty(N, H, N, D, dtype=dtype, device=device)
-    vt = torch.empty(N, H, D, nkp, dtype=dtype, device=device)
-    maskf = torch.empty(N, nkp, dtype=dtype, device=device)
+    vt = torch.empty(N, H, D, nkp, dtype=torch.float16, device=device)
+    maskf = torch.empty(N, nkp, dtype=torch.float16, device=device)
+    # the shared bias is kept in f16, pre-scaled by log2(e) (the attention kernel works in log2 units)
     if Bias_buf is not None and nkp == N and Bias_buf.is_contiguous() and Bias_buf.shape == (H, N, N) \
-            and Bias_buf.dtype == dtype:
+            and Bias_buf.dtype == torch.float16:
         bias = Bias_buf
     else:
-        bias = torch.empty(H, N, nkp, dtype=dtype, device=device)
+        bias = torch.empty(H, N, nkp, dtype=torch.float16, device=device)
     return q, k, vt, maskf, bias
 
 
@@ -134,7 +135,8 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
     """LN + Q/K/V/bias projection of R pair rows X_rows (R, N, C).
 
     Returns dict(q, k, vt, maskf, bias, xln): bias holds this slab's rows of the
-    shared bias, (H, R, Np); the others are row-local attention operands."""
+    shared bias, (H, R, Np) f16 in log2 units; the others are row-local attention
+    operands (vt and maskf f16)."""
     _lib.require_cuda(X_rows)
     R, N2, C = X_rows.shape
     assert N2 == N
@@ -142,8 +144,10 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
     nkp = (N + 7) // 8 * 8
     dev, dty = X_rows.device, X_rows.dtype
     ws = dict(q=torch.empty(R, H, N, D, dtype=dty, device=dev), k=torch.empty(R, H, N, D, dtype=dty, device=dev),
-              vt=torch.empty(R, H, D, nkp, dtype=dty, device=dev), maskf=torch.empty(R, nkp, dtype=dty, device=dev),
-              bias=torch.empty(H, R, nkp, dtype=dty, device=dev), xln=torch.empty(R, N, C, dtype=dty, device=dev))
+              vt=torch.empty(R, H, D, nkp, dtype=torch.float16, device=dev),
+              maskf=torch.empty(R, nkp, dtype=torch.float16, device=dev),
+              bias=torch.empty(H, R, nkp, dtype=torch.float16, device=dev),
+              xln=torch.empty(R, N, C, dtype=dty, device=dev))
     X_rows = X_rows.contiguous()
     m = _mask_u8(mask_rows, (R, N))
     _lib.call("tops_triangle_attn_project", dt, R, N, C, H, D, X_rows.data_ptr(), 1, ln_w.data_ptr(),
