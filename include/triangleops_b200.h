@@ -59,7 +59,7 @@ int tops_selftest_umma(int mode, const void* a, const void* b, float* d, void* s
  *   bz       [H] fp32           bias-projection bias
  *   mask     [N][N] uint8 or NULL (0 = masked key, per row; broadcast over heads/queries)
  *   xln_ws   [N*N][C]           receives x~ (apply_ln=1; else may be NULL)
- *   q_ws,k_ws [N][H][N][D], vt_ws [N][H][D][Np] f16, maskf_ws [N][Np] f16, bias_ws [H][N][Np] f16
+ *   q_ws,k_ws [N][H][N][D] f16, vt_ws [N][H][D][Np] f16, maskf_ws [N][Np] f16, bias_ws [H][N][Np] f16
  *   o_out    [N][N][H*D]        attention output (pre-gate)
  * Supported (C,H,D): (128,4,32), (64,4,16). Rows whose key mask is all zero
  * produce non-finite values (the Python layer patches them to the reference's
@@ -124,7 +124,7 @@ int tops_trimul_forward(int dtype, int direction, int64_t B, int64_t L, int64_t 
  *   x [M][C]; w_qkv [3C][C] rows WQ^T | WK^T | WV^T; z [M][M][Cz] raw pair tensor;
  *   wc [H][Cz] fp32, sum_w [H] fp32, b_const [H] fp32 (LN(z) folded into the bias
  *   projection, attn_pair_bias/module.py:29-35); key_mask [M] uint8 or NULL (extension);
- *   workspaces q_ws, k_ws [H][M][D], vt_ws [H][D][Mp] f16, maskf_ws [Mp] f16, bias_ws [H][M][Mp] fp32.
+ *   workspaces q_ws, k_ws [H][M][D] f16, vt_ws [H][D][Mp] f16, maskf_ws [Mp] f16, bias_ws [H][M][Mp] fp32.
  * Supported: Cz = 128, (C,H,D) in {(128,4,32), (64,4,16)}. */
 int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int64_t D, const void* x,
                      const void* w_qkv, const void* z, const float* wc, const float* sum_w, const float* b_const,

@@ -38,8 +38,8 @@ def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, sca
     dt = _lib.dtype_code(X.dtype)
     mkp = (M + 7) // 8 * 8
     dev = X.device
-    q = torch.empty(1, H, M, D, dtype=X.dtype, device=dev)
-    k = torch.empty(1, H, M, D, dtype=X.dtype, device=dev)
+    q = torch.empty(1, H, M, D, dtype=torch.float16, device=dev)
+    k = torch.empty(1, H, M, D, dtype=torch.float16, device=dev)
     vt = torch.empty(1, H, D, mkp, dtype=torch.float16, device=dev)
     maskf = torch.empty(1, mkp, dtype=torch.float16, device=dev)
     bias = torch.empty(H, M, mkp, dtype=torch.float32, device=dev)

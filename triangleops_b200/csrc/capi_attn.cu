@@ -89,13 +89,13 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nq), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nq) * D * 2};
     const uint32_t box[3] = {D, 128, 1};
-    if (!make_tmap(&mq, dt, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nk), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nk) * D * 2};
     const uint32_t box[3] = {D, Cfg::BK, 1};
-    if (!make_tmap(&mk, dt, 3, k, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, k, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(D), static_cast<uint64_t>(R) * H};
@@ -125,7 +125,7 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
   auto kern = attn_kernel<T, D, TR, TQ, BF32>;
   set_smem(kern, smem);
   dim3 grid((Nq + 128 * TQ - 1) / (128 * TQ), (R + TR - 1) / TR, H);
-  kern<<<grid, 128 + 128 * Cfg::NWG, smem, st>>>(mq, mk, mv, mm, mb, args);
+  kern<<<grid, 128 + 128 * Cfg::NT, smem, st>>>(mq, mk, mv, mm, mb, args);
   return launch_status();
 }
 
@@ -216,7 +216,7 @@ extern "C" int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   const int n = static_cast<int>(N);
-  return run_attn<2, 2>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
+  return run_attn<3, 1>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
                         q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out, static_cast<cudaStream_t>(stream));
 }
 
@@ -241,3 +241,17 @@ extern "C" int tops_fused_gate_forward(int dtype, int64_t T_, int64_t C, const v
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream));
 }
+
+#ifdef TOPS_TRACE
+// Reads (and clears) the attention phase timers: cycles summed over warps for
+// [0] softmax wait on S, [1] S load + f16 convert + bias, [2] max/exp/rescale,
+// [3] PV wait + P store + arrive, [4] issuer wait on K/V and S release,
+// [5] issuer wait on P, [7] producer wait. Built only with -DTOPS_TRACE.
+extern "C" int tops_attn_trace(unsigned long long* out16) {
+  if (cudaMemcpyFromSymbol(out16, tops::g_attn_trace, 16 * sizeof(unsigned long long)) != cudaSuccess)
+    return TOPS_ERR_CUDA;
+  unsigned long long z[16] = {};
+  cudaMemcpyToSymbol(tops::g_attn_trace, z, sizeof(z));
+  return TOPS_OK;
+}
+#endif

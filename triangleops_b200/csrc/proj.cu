@@ -5,9 +5,11 @@
 //
 //   x~  = LN(x) (optional; eps, affine w/b; rounded to the IO dtype and also
 //         written out for the gate stage)                [triangle_attn/module.py:73-79]
-//   Q   = (x~ WQ) * scale   -> Q [R][H][Nk][D]           [triangle_attn/kernel.py:194-195]
+//   Q   = (x~ WQ) * scale   -> Q [R][H][Nk][D]  f16      [triangle_attn/kernel.py:194-195]
 //                              (callers pass scale * log2(e): the attention works in log2 units)
-//   K   =  x~ WK            -> K [R][H][Nk][D]
+//   K   =  x~ WK            -> K [R][H][Nk][D]  f16
+//                              (Q, K, V^T are f16 whatever the IO dtype: they are LN-scale
+//                              projections, and f16 keeps three more mantissa bits than bf16)
 //   V   = (x~ WV) * m[i,k]  -> Vt[R][H][D][Nkp]  f16 (transposed, masked keys zeroed)
 //   m   = mask[i,k] ? 1 : 0 -> maskf[R][Nkp]     f16 (the PV MMA turns it into the row sum)
 //   Bp  = (x~ WZ^T + BZ) * log2(e) -> Bp[H][R][Nkp] f16 (optional) [triangle_attn/kernel.py:36-98]
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t p[D / 2];
 #pragma unroll
           for (int d = 0; d < D / 2; ++d)
-            p[d] = E::pack2(__uint_as_float(r[2 * d]) * a.scale, __uint_as_float(r[2 * d + 1]) * a.scale);
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(a.q) + qk_off);
+            p[d] = Elem<__half>::pack2(__uint_as_float(r[2 * d]) * a.scale, __uint_as_float(r[2 * d + 1]) * a.scale);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.q) + qk_off);
 #pragma unroll
           for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
         }
@@ -241,8 +243,9 @@ __global__ void __launch_bounds__(384, 1)
         if (valid) {
           uint32_t p[D / 2];
 #pragma unroll
-          for (int d = 0; d < D / 2; ++d) p[d] = E::pack2(__uint_as_float(r[2 * d]), __uint_as_float(r[2 * d + 1]));
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(a.k) + qk_off);
+          for (int d = 0; d < D / 2; ++d)
+            p[d] = Elem<__half>::pack2(__uint_as_float(r[2 * d]), __uint_as_float(r[2 * d + 1]));
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.k) + qk_off);
 #pragma unroll
           for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
         }

@@ -36,8 +36,8 @@ def _mask_u8(mask, shape):
 
 def _workspaces(N, C, H, D, dtype, device, Bias_buf=None):
     nkp = (N + 7) // 8 * 8
-    q = torch.empty(N, H, N, D, dtype=dtype, device=device)
-    k = torch.empty(N, H, N, D, dtype=dtype, device=device)
+    q = torch.empty(N, H, N, D, dtype=torch.float16, device=device)
+    k = torch.empty(N, H, N, D, dtype=torch.float16, device=device)
     vt = torch.empty(N, H, D, nkp, dtype=torch.float16, device=device)
     maskf = torch.empty(N, nkp, dtype=torch.float16, device=device)
     # the shared bias is kept in f16, pre-scaled by log2(e) (the attention kernel works in log2 units)
@@ -143,7 +143,8 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
     dt = _lib.dtype_code(X_rows.dtype)
     nkp = (N + 7) // 8 * 8
     dev, dty = X_rows.device, X_rows.dtype
-    ws = dict(q=torch.empty(R, H, N, D, dtype=dty, device=dev), k=torch.empty(R, H, N, D, dtype=dty, device=dev),
+    ws = dict(q=torch.empty(R, H, N, D, dtype=torch.float16, device=dev),
+              k=torch.empty(R, H, N, D, dtype=torch.float16, device=dev),
               vt=torch.empty(R, H, D, nkp, dtype=torch.float16, device=dev),
               maskf=torch.empty(R, nkp, dtype=torch.float16, device=dev),
               bias=torch.empty(H, R, nkp, dtype=torch.float16, device=dev),
@@ -161,9 +162,10 @@ def attend_rows(ws, bias_full, H, D, out=None):
     """Flash attention of the R projected rows in ``ws`` against the full shared bias
     (H, N, Np) -> O (R, N, H*D)."""
     R, _, N, _ = ws["q"].shape
-    dt = _lib.dtype_code(ws["q"].dtype)
+    io = ws["xln"].dtype  # Q/K/V^T workspaces are f16; the output is in the IO dtype
+    dt = _lib.dtype_code(io)
     if out is None:
-        out = torch.empty(R, N, H * D, dtype=ws["q"].dtype, device=ws["q"].device)
+        out = torch.empty(R, N, H * D, dtype=io, device=ws["q"].device)
     _lib.call("tops_triangle_attn_attend", dt, R, N, H, D, ws["q"].data_ptr(), ws["k"].data_ptr(),
               ws["vt"].data_ptr(), ws["maskf"].data_ptr(), bias_full.data_ptr(), out.data_ptr(),
               _lib.stream_ptr(out.device))
