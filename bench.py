@@ -228,6 +228,39 @@ def other_ops(dev):
     return out
 
 
+def profile_op(args):
+    """Run one of the other ops alone (for ncu captures): triangle_mul incoming at L = --n
+    (config 3 generator) or attn_pair_bias at M = --n (config 2 generator)."""
+    import triangleops_b200 as tops
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def rn(*s, sd=1.0):
+        return (torch.randn(*s, generator=g, device=dev) * sd).to(torch.bfloat16)
+
+    n = args.n
+    if args.profile_op == "triangle_mul":
+        x = rn(1, n, n, C)
+        v = torch.zeros(n, device=dev)
+        v[: n * 1900 // 2048] = 1
+        mask = (v[:, None] * v[None, :])[None]
+        w = [1 + 0.1 * rn(C), 0.1 * rn(C), rn(2 * C, C, sd=C**-0.5), rn(2 * C, C, sd=C**-0.5), 1 + 0.1 * rn(C),
+             0.1 * rn(C), rn(C, C, sd=C**-0.5), rn(C, C, sd=C**-0.5)]
+        pre = tops.triangle_mul.precompute(*w)
+        fn = lambda: tops.triangle_mul.forward(x, pre, direction="incoming", mask=mask)  # noqa: E731
+    else:
+        X, Z = rn(n, C), rn(n, n, C)
+        Wq, Wk, Wv, Wg, Wo = (rn(C, C, sd=C**-0.5) for _ in range(5))
+        pre = tops.attn_pair_bias.precompute(Wq, Wk, Wv, 1 + 0.1 * rn(C), 0.1 * rn(C), rn(C, H, sd=C**-0.5), None, H, D)
+        km = torch.ones(n, dtype=torch.bool, device=dev)
+        km[-64:] = False
+        fn = lambda: tops.attn_pair_bias.forward(X, Z, pre, scale=1.0, W_proj_g=Wg, B_proj_g=None, W_proj_o=Wo,  # noqa
+                                                 B_proj_o=None, mask=km)
+    ms = time_op(fn, iters=args.steps, warmup=args.warmup)
+    print(json.dumps({"profile_op": args.profile_op, "n": n, "ms": ms}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -237,9 +270,13 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEF)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ops", action="store_true", help="skip the other two ops")
+    ap.add_argument("--profile-op", choices=["triangle_mul", "attn_pair_bias"], default=None,
+                    help="run only this op (config 3 / config 2 shapes at --n) for profiling, print its time")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_op:
+        return profile_op(args)
 
     import torch.distributed as dist
 
@@ -346,14 +383,10 @@ def main():
             threads = os.cpu_count() or 1
             cms, sample = cpu_oracle_ms(inp, N, threads)
             cpu = {"value": cms, "unit": "ms", "cores": threads, "kind": "port", "sample": sample}
-        traffic = None
-        tpath = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tpath):
-            try:
-                tj = json.load(open(tpath))
-                traffic = tj.get("attn_kernel_bytes_per_launch_N2048") * (n / N)
-            except Exception:
-                traffic = None
+        # DRAM bytes per attention launch from ncu at N=1024 (profiles/
+        # attn_kernel_triangle_attention_n1024.md: 823 MB read + 256 MB written), scaled by
+        # rows x keys (n * N) — the kernel streams Q/K/V once and writes O once.
+        traffic = 1.0791e9 * (n * N) / (1024 * 1024)
         line = {
             "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)",
             "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
