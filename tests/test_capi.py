@@ -70,3 +70,13 @@ def test_no_cpu_fallback():
                                         ("p_out_weight", (128, 128)), ("g_out_weight", (128, 128)))}
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         tops.triangle_multiplicative_update(x.bfloat16(), direction="outgoing", **w)
+
+
+def test_drop_in_import_name():
+    import triangle_ops
+    import triangle_ops.triangle_mul as tm
+
+    assert triangle_ops.triangle_attention is not None
+    assert tm.precompute is triangle_ops.triangle_mul.precompute
+    for name in ("triangle_attention", "triangle_multiplicative_update", "attention_pair_bias"):
+        assert hasattr(triangle_ops, name)
