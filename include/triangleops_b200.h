@@ -103,6 +103,14 @@ int tops_trimul_input_phase(int dtype, int64_t M, int64_t C, const void* x, cons
  *   a, b, y [nb][L][L]; L % 8 == 0. */
 int tops_trimul_contract(int dtype, int direction, int64_t nb, int64_t L, const void* a, const void* b, void* y,
                          void* stream);
+/* Row-slab contraction for sharded runs (no counterpart in the single-device reference;
+ * the einsum of triangle_mul/module.py:70-76 restricted to Mi output rows):
+ *   a [nb][Mi][L] (outgoing) or [nb][L][Mi] (incoming) — this rank's rows i;
+ *   b = P rank-major chunks as all_gather_into_tensor lays them out:
+ *       [P][nb][L/P][L] (outgoing: rows j, K = k) or [P][nb][L][L/P] (incoming: M = j);
+ *   y [nb][Mi][L]. L % P == 0 and (L/P) % 128 == 0 when P > 1; Mi % 8 == 0. */
+int tops_trimul_contract_slab(int dtype, int direction, int64_t nb, int64_t Mi, int64_t L, int64_t P, const void* a,
+                              const void* b, void* y, void* stream);
 /* Output phase — replaces triangle_mul/kernel.py:282-326 (output_phase):
  *   out[m][c] = sigmoid(LN_in(x) g_out^T)[m,c] * (LN_out(y) p_out^T)[m,c]
  *   y [C][M] (D-major), x [M][C]; w_out [2C][C] = p_out_c | g_out_c; sum_out, b_out [2C] fp32;

@@ -67,6 +67,77 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+class CpuTrimulOps:
+    """fp32 torch stand-ins for the triangle-mul kernels (same layouts)."""
+
+    @staticmethod
+    def input_phase(xt, mt, pre, eps):
+        w = pre["w"]
+        C = xt.shape[1]
+        xln = F.layer_norm(xt, (C,), w["norm_in_weight"], w["norm_in_bias"], eps)
+        g = F.linear(xln, w["p_in_weight"]) * F.linear(xln, w["g_in_weight"]).sigmoid()
+        if mt is not None:
+            g = g * mt.float()[:, None]
+        return g.t().contiguous()  # (2C, M)
+
+    @staticmethod
+    def contract_slab(a, b_chunks, direction, Mi, L, P):
+        if direction == "outgoing":  # a (C, Mi, L); b_chunks (P, C, L/P, L)
+            b = b_chunks.permute(1, 0, 2, 3).reshape(a.shape[0], L, L)
+            return torch.einsum("dik,djk->dij", a, b)
+        b = b_chunks.permute(1, 2, 0, 3).reshape(a.shape[0], L, L)  # (C, k, j)
+        return torch.einsum("dki,dkj->dij", a, b)
+
+    @staticmethod
+    def output_phase(y, xt, pre, eps):
+        w = pre["w"]
+        C = xt.shape[1]
+        yt = y.t()
+        yln = F.layer_norm(yt, (C,), w["norm_out_weight"], w["norm_out_bias"], eps)
+        xln = F.layer_norm(xt, (C,), w["norm_in_weight"], w["norm_in_bias"], eps)
+        return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
+
+
+def _trimul_inputs():
+    g = torch.Generator().manual_seed(11)
+    L, C = 8, 16
+    r = lambda *s, sd=1.0: torch.randn(*s, generator=g) * sd  # noqa: E731
+    w = dict(norm_in_weight=1 + 0.1 * r(C), norm_in_bias=0.1 * r(C), p_in_weight=r(2 * C, C, sd=C**-0.5),
+             g_in_weight=r(2 * C, C, sd=C**-0.5), norm_out_weight=1 + 0.1 * r(C), norm_out_bias=0.1 * r(C),
+             p_out_weight=r(C, C, sd=C**-0.5), g_out_weight=r(C, C, sd=C**-0.5))
+    return r(1, L, L, C), (torch.rand(1, L, L, generator=g) > 0.2), w
+
+
+def _trimul_worker(rank, world, port, q, direction):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, mask, w = _trimul_inputs()
+        out = tdist.triangle_multiplicative_update_rows(x, {"w": w}, direction=direction, mask=mask, ops=CpuTrimulOps)
+        full = tdist.all_gather_rows(out[0].contiguous(), 0)
+        if rank == 0:
+            q.put(full)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("direction", ["outgoing", "incoming"])
+def test_sharded_triangle_mul_gloo(direction):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_trimul_worker, args=(r, 2, port, q, direction)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, mask, w = _trimul_inputs()
+    ref = oracle.triangle_multiplicative_update(x, direction=direction, mask=mask, **w)
+    assert (full - ref[0]).abs().max().item() < 1e-4
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

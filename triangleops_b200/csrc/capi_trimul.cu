@@ -42,24 +42,39 @@ int launch_trimul_out(int dtype, const void* y, const void* x, const void* w, co
 }
 
 template <typename T, bool MN>
-int launch_contract(int dtype, int nb, int L, const void* a, const void* b, void* y, cudaStream_t st) {
+int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, const void* b, void* y, cudaStream_t st) {
   CUtensorMap ma, mb;
-  const uint64_t dims[3] = {static_cast<uint64_t>(L), static_cast<uint64_t>(L), static_cast<uint64_t>(nb)};
-  const uint64_t str[2] = {static_cast<uint64_t>(L) * 2, static_cast<uint64_t>(L) * L * 2};
+  const int nc = L / P;
+  const uint64_t e = 2;
   if (!MN) {
-    const uint32_t ba[3] = {kCtBK, kCtBM, 1}, bb[3] = {kCtBK, kCtBN, 1};
-    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, dims, str, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
-    if (!make_tmap(&mb, tmap_dtype(dtype), 3, b, dims, str, bb, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    // A [nb][Mi][L] (K = L contiguous); B: P chunks of [nb][nc][L]
+    const uint64_t da[3] = {static_cast<uint64_t>(L), static_cast<uint64_t>(Mi), static_cast<uint64_t>(nb)};
+    const uint64_t sa[2] = {L * e, static_cast<uint64_t>(Mi) * L * e};
+    const uint32_t ba[3] = {kCtBK, kCtBM, 1};
+    const uint64_t db[4] = {static_cast<uint64_t>(L), static_cast<uint64_t>(nc), static_cast<uint64_t>(nb),
+                            static_cast<uint64_t>(P)};
+    const uint64_t sb[3] = {L * e, static_cast<uint64_t>(nc) * L * e, static_cast<uint64_t>(nb) * nc * L * e};
+    const uint32_t bbx[4] = {kCtBK, 128, 1, 1};
+    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   } else {
+    // A [nb][L][Mi] (M = i contiguous); B: P chunks of [nb][L][nc]
+    const uint64_t da[3] = {static_cast<uint64_t>(Mi), static_cast<uint64_t>(L), static_cast<uint64_t>(nb)};
+    const uint64_t sa[2] = {static_cast<uint64_t>(Mi) * e, static_cast<uint64_t>(Mi) * L * e};
     const uint32_t bx[3] = {64, kCtBK, 1};
-    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, dims, str, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
-    if (!make_tmap(&mb, tmap_dtype(dtype), 3, b, dims, str, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    const uint64_t db[4] = {static_cast<uint64_t>(nc), static_cast<uint64_t>(L), static_cast<uint64_t>(nb),
+                            static_cast<uint64_t>(P)};
+    const uint64_t sb[3] = {static_cast<uint64_t>(nc) * e, static_cast<uint64_t>(nc) * L * e,
+                            static_cast<uint64_t>(nb) * nc * L * e};
+    const uint32_t bbx[4] = {64, kCtBK, 1, 1};
+    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
-  CtArgs args{L, nb, y};
+  CtArgs args{L, nb, y, Mi, nc};
   const size_t smem = sizeof(CtSmem) + 1024;
   auto kern = trimul_contract_kernel<T, MN>;
   set_smem(kern, smem);
-  const long long tiles = static_cast<long long>((L + kCtBM - 1) / kCtBM) * ((L + kCtBN - 1) / kCtBN) * nb;
+  const long long tiles = static_cast<long long>((Mi + kCtBM - 1) / kCtBM) * ((L + kCtBN - 1) / kCtBN) * nb;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
   kern<<<grid, 256, smem, st>>>(ma, mb, args);
   return launch_status();
@@ -88,12 +103,13 @@ int run_trimul_out(int dtype, int C, const void* y, const void* x, const void* w
   return TOPS_ERR_SHAPE;
 }
 
-int run_contract(int dtype, int direction, int nb, int L, const void* a, const void* b, void* y, cudaStream_t st) {
+int run_contract(int dtype, int direction, int nb, int Mi, int L, int P, const void* a, const void* b, void* y,
+                 cudaStream_t st) {
   if (dtype == TOPS_BF16)
-    return direction == 0 ? launch_contract<__nv_bfloat16, false>(dtype, nb, L, a, b, y, st)
-                          : launch_contract<__nv_bfloat16, true>(dtype, nb, L, a, b, y, st);
-  return direction == 0 ? launch_contract<__half, false>(dtype, nb, L, a, b, y, st)
-                        : launch_contract<__half, true>(dtype, nb, L, a, b, y, st);
+    return direction == 0 ? launch_contract<__nv_bfloat16, false>(dtype, nb, Mi, L, P, a, b, y, st)
+                          : launch_contract<__nv_bfloat16, true>(dtype, nb, Mi, L, P, a, b, y, st);
+  return direction == 0 ? launch_contract<__half, false>(dtype, nb, Mi, L, P, a, b, y, st)
+                        : launch_contract<__half, true>(dtype, nb, Mi, L, P, a, b, y, st);
 }
 
 }  // namespace tops
@@ -121,8 +137,26 @@ extern "C" int tops_trimul_contract(int dtype, int direction, int64_t nb, int64_
   const void* ptrs[] = {a, b, y};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
-  return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(L), a, b, y,
+  return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(L), static_cast<int>(L), 1, a, b, y,
                       static_cast<cudaStream_t>(stream));
+}
+
+// Row-slab contraction for sharded runs: this rank's Mi output rows against the
+// all-gathered B, which is laid out as P rank-major chunks of L/P columns
+// (exactly what all_gather_into_tensor produces). See the header for layouts.
+extern "C" int tops_trimul_contract_slab(int dtype, int direction, int64_t nb, int64_t Mi, int64_t L, int64_t P,
+                                         const void* a, const void* b, void* y, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (direction != 0 && direction != 1) return TOPS_ERR_ARG;
+  if (nb <= 0 || L <= 0 || Mi <= 0 || P <= 0 || Mi > L || nb >= (1 << 30) || L >= (1 << 20)) return TOPS_ERR_SHAPE;
+  if (L % P != 0) return TOPS_ERR_SHAPE;
+  if (L % 8 != 0 || Mi % 8 != 0) return TOPS_ERR_ALIGN;
+  if (P > 1 && (L / P) % 128 != 0) return TOPS_ERR_SHAPE;  // a 128-row B box stays inside one chunk
+  const void* ptrs[] = {a, b, y};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(Mi), static_cast<int>(L),
+                      static_cast<int>(P), a, b, y, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const void* y, const void* x,

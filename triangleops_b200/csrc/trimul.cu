@@ -245,7 +245,9 @@ struct CtSmem {
 
 struct CtArgs {
   int L, nb;
-  void* y;  // [nb][L][L]
+  void* y;  // [nb][Mi][L]
+  int Mi;   // rows of A / y (L unsharded; a row slab of size L/P when sharded)
+  int nc;   // extent of one B chunk along j (B is P rank-major chunks of nc columns; nc = L unsharded)
 };
 
 template <typename T, bool MN>
@@ -256,7 +258,7 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ uint8_t smem_raw[];
   CtSmem& sm = *reinterpret_cast<CtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nI = (a.L + kCtBM - 1) / kCtBM, nJ = (a.L + kCtBN - 1) / kCtBN;
+  const int nI = (a.Mi + kCtBM - 1) / kCtBM, nJ = (a.L + kCtBN - 1) / kCtBN;
   const long long n_tiles = static_cast<long long>(nI) * nJ * a.nb;
   const int nk = (a.L + kCtBK - 1) / kCtBK;
   if (threadIdx.x == 0) {
@@ -301,10 +303,18 @@ __global__ void __launch_bounds__(256, 1)
           const int k0 = kb * kCtBK;
           if (!MN) {
             tma_load_3d(sm.a[s], &map_a, &sm.full[s], k0, i0, bb);
-            tma_load_3d(sm.b[s], &map_b, &sm.full[s], k0, j0, bb);
+            // B rows j live in rank-major chunks of nc rows: (j mod nc, chunk j / nc);
+            // j >= L lands on chunk >= P, which the tensor map zero-fills.
+            for (int h = 0; h < kCtBN / 128; ++h) {
+              const int j = j0 + h * 128, ch = j / a.nc;
+              tma_load_4d(sm.b[s] + h * 16384, &map_b, &sm.full[s], k0, j - ch * a.nc, bb, ch);
+            }
           } else {
             for (int h = 0; h < kCtBM / 64; ++h) tma_load_3d(sm.a[s] + h * 8192, &map_a, &sm.full[s], i0 + h * 64, k0, bb);
-            for (int h = 0; h < kCtBN / 64; ++h) tma_load_3d(sm.b[s] + h * 8192, &map_b, &sm.full[s], j0 + h * 64, k0, bb);
+            for (int h = 0; h < kCtBN / 64; ++h) {
+              const int j = j0 + h * 64, ch = j / a.nc;
+              tma_load_4d(sm.b[s] + h * 8192, &map_b, &sm.full[s], j - ch * a.nc, k0, bb, ch);
+            }
           }
         }
         if (!ok) break;
@@ -354,12 +364,12 @@ __global__ void __launch_bounds__(256, 1)
       int bb, i0, j0;
       decode(tile, bb, i0, j0);
       const int i = i0 + row;
-      T* dst = static_cast<T*>(a.y) + (static_cast<size_t>(bb) * a.L + i) * a.L + j0;
+      T* dst = static_cast<T*>(a.y) + (static_cast<size_t>(bb) * a.Mi + i) * a.L + j0;
 #pragma unroll 1
       for (int c0 = 0; c0 < kCtBN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + acc * 256 + c0, r);
-        if (i < a.L) {
+        if (i < a.Mi) {
           uint32_t p[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) p[e] = E::pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));

@@ -9,6 +9,12 @@ only where the algorithm exchanges data:
   Bp come out of the same GEMM), the Bp slabs are all-gathered, then attention and
   the gate run on local rows. Per rank the exchange is H*N*N*(P-1)/P elements
   (29 MB at N=2048, P=8).
+* triangle multiplicative update (x replicated, as in the 1/2/4/8-GPU configuration):
+  output row i needs a[., i, .] (outgoing: row i of a; incoming: column i of a) and
+  ALL of b. Each rank runs the input phase on the token slab that yields its a and
+  its share of b (outgoing: pair rows of the slab; incoming: pair columns), b is
+  all-gathered (C*L*L*(P-1)/P elements per rank), then the row-slab contraction
+  reads the gathered chunks in place and the output phase runs on the rank's rows.
 
 The per-rank compute steps are looked up on an ``ops`` object so that the host
 logic (slab partitioning, collective assembly) is testable with gloo on CPU.
@@ -78,3 +84,56 @@ def triangle_attention_rows(X_rows, pre, *, N, mask_rows=None, scale=1.0, eps=1e
         w = pre["W_qkvz"]
         _fix_fully_masked_rows(O, ws["xln"], w[2 * H * D:3 * H * D].t(), mask_rows, H, D)
     return ops.gate(O, ws, W_proj_g, W_proj_o)
+
+
+class TrimulKernelOps:
+    """The sm_100a kernels for one rank's triangle-mul slab."""
+
+    @staticmethod
+    def input_phase(x_tokens, mask_tokens, pre, eps):
+        from .triangle_mul.kernel import input_phase_tokens
+
+        return input_phase_tokens(x_tokens, mask_tokens, pre, eps)
+
+    @staticmethod
+    def contract_slab(a, b_chunks, direction, Mi, L, P):
+        from .triangle_mul.kernel import contract_slab
+
+        return contract_slab(a, b_chunks, direction, Mi, L, P)
+
+    @staticmethod
+    def output_phase(y, x_tokens, pre, eps):
+        from .triangle_mul.kernel import output_phase_tokens
+
+        return output_phase_tokens(y, x_tokens, pre, eps)
+
+
+def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-5, group=None, ops=TrimulKernelOps):
+    """Rows [r0, r1) of the triangle multiplicative update of the replicated pair tensor
+    x (1, L, L, C); returns (1, n, L, C). Collective: all-gather of this rank's b."""
+    if direction not in ("outgoing", "incoming"):
+        raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
+    B, L, _, C = x.shape
+    assert B == 1, "row-slab sharding takes one pair tensor"
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    r0, r1 = slab(L, rank, world)
+    n = r1 - r0
+    if direction == "outgoing":  # a rows i in slab, b rows j in slab: tokens (i, k)
+        xs = x[0, r0:r1].reshape(n * L, C)
+        ms = None if mask is None else mask.reshape(L, L)[r0:r1].reshape(n * L)
+    else:  # a columns i in slab, b columns j in slab: tokens (k, i)
+        xs = x[0, :, r0:r1].contiguous().reshape(L * n, C)
+        ms = None if mask is None else mask.reshape(L, L)[:, r0:r1].contiguous().reshape(L * n)
+    ab = ops.input_phase(xs.contiguous(), ms, pre, eps)  # (2C, n*L) as [d][i][k] or [d][k][i]
+    a = ab[:C].reshape(C, n, L) if direction == "outgoing" else ab[:C].reshape(C, L, n)
+    b = ab[C:].reshape(C, n, L) if direction == "outgoing" else ab[C:].reshape(C, L, n)
+    if world > 1:
+        flat = torch.empty((world * b.shape[0],) + tuple(b.shape[1:]), dtype=b.dtype, device=b.device)
+        dist.all_gather_into_tensor(flat, b.contiguous(), group=group)  # rank-major concatenation
+        b_chunks = flat.view((world,) + tuple(b.shape))
+    else:
+        b_chunks = b.unsqueeze(0)
+    y = ops.contract_slab(a, b_chunks, direction, n, L, world)  # (C, n, L)
+    out = ops.output_phase(y.reshape(C, n * L), x[0, r0:r1].reshape(n * L, C).contiguous(), pre, eps)
+    return out.reshape(1, n, L, C)

@@ -17,6 +17,7 @@ from .. import _lib
 _P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _lib.register("tops_trimul_input_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P])
 _lib.register("tops_trimul_contract", [_I, _I, _I64, _I64, _P, _P, _P, _P])
+_lib.register("tops_trimul_contract_slab", [_I, _I, _I64, _I64, _I64, _I64, _P, _P, _P, _P])
 _lib.register("tops_trimul_output_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P])
 _lib.register("tops_trimul_forward",
               [_I, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P])
@@ -119,4 +120,44 @@ def fused_forward(x, pre, direction, mask=None, eps=1e-5, out=None, ab_ws=None, 
               pre["sum_in"].data_ptr(), pre["b_in"].data_ptr(), w_out.data_ptr(), pre["sum_out"].data_ptr(),
               pre["b_out"].data_ptr(), float(eps), ab_ws.data_ptr(), y_ws.data_ptr(), out.data_ptr(),
               _lib.stream_ptr(x.device))
+    return out
+
+
+def input_phase_tokens(x_tokens, mask_tokens, pre, eps=1e-5):
+    """Input phase over an arbitrary contiguous token set x_tokens (M, C) -> ab (2C, M)."""
+    _lib.require_cuda(x_tokens)
+    M, C = x_tokens.shape
+    dt = _lib.dtype_code(x_tokens.dtype)
+    w_in = pre["w_in"] if pre["w_in"].dtype == x_tokens.dtype else pre["w_in"].to(x_tokens.dtype)
+    out = torch.empty(2 * C, M, device=x_tokens.device, dtype=x_tokens.dtype)
+    m = mask_u8(mask_tokens, M)
+    _lib.call("tops_trimul_input_phase", dt, M, C, x_tokens.data_ptr(), _lib.ptr(m), w_in.data_ptr(),
+              pre["sum_in"].data_ptr(), pre["b_in"].data_ptr(), float(eps), out.data_ptr(),
+              _lib.stream_ptr(x_tokens.device))
+    return out
+
+
+def contract_slab(a, b_chunks, direction, Mi, L, P):
+    """Row-slab contraction: a (C, Mi, L) outgoing / (C, L, Mi) incoming; b_chunks the
+    all-gathered (P, C, L/P, L) / (P, C, L, L/P). Returns y (C, Mi, L)."""
+    code = direction_code(direction)
+    C = a.shape[0]
+    dt = _lib.dtype_code(a.dtype)
+    y = torch.empty(C, Mi, L, device=a.device, dtype=a.dtype)
+    a = a.contiguous()
+    b_chunks = b_chunks.contiguous()
+    _lib.call("tops_trimul_contract_slab", dt, code, C, Mi, L, P, a.data_ptr(), b_chunks.data_ptr(), y.data_ptr(),
+              _lib.stream_ptr(a.device))
+    return y
+
+
+def output_phase_tokens(y_dmajor, x_tokens, pre, eps=1e-5):
+    """Output phase: y (C, M) D-major and x_tokens (M, C) -> (M, C)."""
+    M, C = x_tokens.shape
+    dt = _lib.dtype_code(x_tokens.dtype)
+    w_out = pre["w_out"] if pre["w_out"].dtype == x_tokens.dtype else pre["w_out"].to(x_tokens.dtype)
+    out = torch.empty(M, C, device=x_tokens.device, dtype=x_tokens.dtype)
+    _lib.call("tops_trimul_output_phase", dt, M, C, y_dmajor.data_ptr(), x_tokens.data_ptr(), w_out.data_ptr(),
+              pre["sum_out"].data_ptr(), pre["b_out"].data_ptr(), float(eps), out.data_ptr(),
+              _lib.stream_ptr(x_tokens.device))
     return out
