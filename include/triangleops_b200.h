@@ -153,6 +153,32 @@ int tops_apb_forward_noalloc(int dtype, int64_t M, int64_t C, int64_t Cz, int64_
                              const float* b_const, const uint8_t* key_mask, float scale, float eps, void* og_out,
                              void* stream);
 
+/* ---------------------------------------------------------------------------
+ * fp32 IO path (CUDA cores). The reference admits fp32 IO for all three ops
+ * (_common/dtype.py:7-19) and then runs its Triton kernels in fp32; these four
+ * generic kernels are what the package composes each op's fp32 forward from
+ * (triangleops_b200/_f32.py). All pointers fp32 unless noted. */
+
+/* y[t][c] = LN(x[t])[c] * w[c] + b[c] over rows of width C; w, b may be NULL. */
+int tops_f32_layernorm(int64_t T, int64_t C, const float* x, const float* w, const float* b, float eps, float* y,
+                       void* stream);
+
+/* Batched strided C(b,m,n) = sum_k A(b,m,k) B(b,n,k) + bias[n] (bias may be NULL).
+ * strides[9] = {A: b, m, k; B: b, n, k; C: b, m, n} in elements. */
+int tops_f32_gemm(int64_t batch, int64_t M, int64_t N, int64_t K, const float* A, const float* B, const float* bias,
+                  float* C, const int64_t* strides, void* stream);
+
+/* O[r][q][h*D+d] = softmax_k(scale * q.k + bias[h][q][k]) v, D in {16, 32}.
+ * q/k/v element (r,h,n,d) at r*sr + h*sh + n*sn + d; mask [R][Nk] uint8 or NULL;
+ * mask_mode 0: masked keys get -1e9 added (triangle attention); 1: masked keys dropped. */
+int tops_f32_attention(int64_t R, int64_t H, int64_t Nq, int64_t Nk, int64_t D, const float* q, const float* k,
+                       const float* v, int64_t sr, int64_t sh, int64_t sn, const float* bias, const uint8_t* mask,
+                       float scale, int mask_mode, float* out, void* stream);
+
+/* y[r][c] = a[r][c] * sigmoid(g[r][c] + bg[c]) * mask[r]; bg, mask (0/1 bytes) may be NULL. */
+int tops_f32_gated_mul(int64_t rows, int64_t cols, const float* a, int64_t lda, const float* g, int64_t ldg,
+                       const float* bg, const uint8_t* mask, float* y, int64_t ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

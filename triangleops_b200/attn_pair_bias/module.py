@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 
 from .._common.layouts import interleave_qkv, qkv_rows
+from .. import _f32
 from .._common.ln_absorption import absorb_ln_matmul
 from ..triangle_attn.kernel import gate_forward
 from .kernel import apb_core
@@ -33,6 +34,8 @@ def precompute(WQ, WK, WV, W_ln, B_ln, W_proj_z, B_proj_z, H, D):
         "w_rows": qkv_rows(WQ, WK, WV),
         "H": H,
         "D": D,
+        # fp32 IO path: the unfolded weights
+        "f32": (WQ, WK, WV, W_ln, B_ln, W_proj_z, B_proj_z),
     }
 
 
@@ -40,6 +43,10 @@ def forward(X, Z, pre, *, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_proj_o, B_p
     """Per-call forward (``module.py:45-66``). X (M, c_s), Z (M, M, C_z) -> (M, c_s)."""
     M = X.shape[0]
     H, D = pre["H"], pre["D"]
+    if X.dtype == torch.float32:
+        WQ, WK, WV, W_ln, B_ln, W_pz, B_pz = pre["f32"]
+        return _f32.attention_pair_bias(X, WQ, WK, WV, Z, W_ln, B_ln, W_pz, B_pz, W_proj_g, B_proj_g, W_proj_o,
+                                        B_proj_o, H, D, scale, eps, mask)
     w = pre["w_rows"]
     if w.dtype != X.dtype:
         w = w.to(X.dtype)

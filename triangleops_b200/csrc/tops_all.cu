@@ -11,3 +11,4 @@
 #include "zbias.cu"
 #include "capi_apb.cu"
 #include "noalloc.cu"
+#include "f32.cu"

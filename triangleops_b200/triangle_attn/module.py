@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import torch
 
+from .. import _f32
 from .._common.layouts import interleave_kv, qkv_rows
 from .kernel import gate_forward, triangle_attn_fused_forward
 
@@ -42,6 +43,8 @@ def precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D):
         "ln_b32": ln_b,
         "H": H,
         "D": D,
+        # fp32 IO path: the unfolded weights
+        "f32": (W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z),
     }
 
 
@@ -67,6 +70,8 @@ def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_pro
     )
     H, D = pre["H"], pre["D"]
     N = X.shape[0]
+    if X.dtype == torch.float32:
+        return _f32.triangle_attention(X, *pre["f32"], W_proj_g, W_proj_o, H, D, scale, eps, mask)
     w = pre["W_qkvz"]
     if w.dtype != X.dtype:
         w = w.to(X.dtype)

@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
+from .. import _f32
 from .._common.ln_absorption import absorb_ln
 from .kernel import direction_code, fused_forward
 
@@ -46,6 +47,10 @@ def precompute(norm_in_weight, norm_in_bias, p_in_weight, g_in_weight, norm_out_
         "w_out": torch.cat([p_out_c, g_out_c], 0).contiguous(),
         "sum_out": torch.cat([sWp_out, sWg_out]).contiguous(),
         "b_out": torch.cat([Bp_out, Bg_out]).contiguous(),
+        # fp32 IO path: the unfolded weights
+        "f32": {"norm_in_weight": norm_in_weight, "norm_in_bias": norm_in_bias, "p_in_weight": p_in_weight,
+                "g_in_weight": g_in_weight, "norm_out_weight": norm_out_weight, "norm_out_bias": norm_out_bias,
+                "p_out_weight": p_out_weight, "g_out_weight": g_out_weight},
     }
 
 
@@ -53,6 +58,8 @@ def forward(x, pre, *, direction, mask=None, eps=1e-5):
     """Per-call forward (``module.py:55-88``). x (B, L, L, C) -> (B, L, L, C)."""
     direction_code(direction)  # ValueError on an unknown direction, before any launch
     B, L, _, C = x.shape
+    if x.dtype == torch.float32:
+        return _f32.triangle_multiplicative_update(x, pre["f32"], direction, mask, eps)
     Lp = (L + 7) // 8 * 8
     if Lp == L:
         return fused_forward(x, pre, direction, mask=mask, eps=eps)
