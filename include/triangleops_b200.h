@@ -139,6 +139,16 @@ int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int
                      const uint8_t* key_mask, float scale, float eps, void* q_ws, void* k_ws, void* vt_ws,
                      void* maskf_ws, void* bias_ws, void* og_out, void* stream);
 
+/* Query rows [q0, q0 + Mq) of tops_apb_forward (row-sharded pair-bias attention; the
+ * reference is single-device, its kernel tiles queries the same way, attn_pair_bias/kernel.py:229).
+ * x [M][C] is the whole sequence (K/V need every key); z_rows [Mq][M][Cz] are the pair rows
+ * of those queries; bias_ws [H][Mq][Mp] fp32; og_rows [Mq][H*D]; q_ws/k_ws/vt_ws/maskf_ws
+ * as for tops_apb_forward (full M). tops_apb_forward is q0 = 0, Mq = M. */
+int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t Mq, int64_t C, int64_t Cz, int64_t H, int64_t D,
+                          const void* x, const void* w_qkv, const void* z_rows, const float* wc, const float* sum_w,
+                          const float* b_const, const uint8_t* key_mask, float scale, float eps, void* q_ws,
+                          void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws, void* og_rows, void* stream);
+
 /* No counterpart in the reference. tops_apb_forward for callers that cannot
  * allocate device memory (a serving runtime or embedding framework that owns a
  * fixed device-memory budget and forbids allocation after start-up): same

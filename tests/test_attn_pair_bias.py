@@ -89,3 +89,22 @@ def test_lowlevel_apb_forward(device):
     ref = oracle.attention_pair_bias(*args, scale=1.0)
     rio = oracle.attention_pair_bias(*args, scale=1.0, io_round=torch.bfloat16)
     assert_parity(out, ref, torch.bfloat16, "low-level", ref_io=rio)
+
+
+@pytest.mark.parametrize("M", [256, 1000])
+def test_query_row_windows(device, M):
+    """tops_apb_forward_rows: query windows (ragged, unaligned starts) of the row-sharded
+    entry point reproduce the corresponding rows of the whole-sequence call."""
+    from triangleops_b200.attn_pair_bias.kernel import apb_core
+
+    args = _inputs(M, torch.bfloat16, device, general=True)
+    (X, WQ, WK, WV, Z, W_ln, B_ln, W_pz, B_pz, W_pg, B_pg, W_po, B_po, H, D) = args
+    km = torch.ones(M, dtype=torch.bool, device=device)
+    km[-24:] = False
+    pre = tops.attn_pair_bias.precompute(WQ, WK, WV, W_ln, B_ln, W_pz, B_pz, H, D)
+    core = lambda Zr, Og, q0: apb_core(X, pre["w_rows"], Zr, pre["W_combined"], pre["sum_W_combined"],  # noqa: E731
+                                       pre["B_const"], Og, H, D, key_mask=km, q0=q0)
+    full = core(Z, torch.empty(M, H * D, device=device, dtype=X.dtype), 0)
+    for q0, q1 in ((0, M // 2), (M // 2, M), (37, 37 + 131), (M - 5, M)):
+        part = core(Z[q0:q1], torch.empty(q1 - q0, H * D, device=device, dtype=X.dtype), q0)
+        assert torch.equal(part, full[q0:q1]), f"window [{q0}, {q1})"

@@ -165,3 +165,72 @@ def test_sharded_triangle_attention_gloo():
     ref = oracle.triangle_attention(a["X"], a["W_ln"], a["B_ln"], a["WQ"], a["WK"], a["WV"], a["Wz"], a["BZ"],
                                     a["Wg"], None, a["Wo"], None, H, D, scale=D**-0.5, mask=mask)
     assert (full - ref).abs().max().item() < 1e-4
+
+
+class CpuApbOps:
+    """fp32 torch stand-ins for the pair-bias attention kernels (query rows q0..)."""
+
+    @staticmethod
+    def attend_rows(X, Z_rows, pre, q0, scale, eps, key_mask):
+        w = pre["w"]
+        H, D = pre["H"], pre["D"]
+        M, n = X.shape[0], Z_rows.shape[0]
+        q = (X[q0:q0 + n] @ w["WQ"]).view(n, H, D).transpose(0, 1)
+        k = (X @ w["WK"]).view(M, H, D).transpose(0, 1)
+        v = (X @ w["WV"]).view(M, H, D).transpose(0, 1)
+        bias = (F.layer_norm(Z_rows, Z_rows.shape[-1:], w["W_ln"], w["B_ln"], eps) @ w["Wz"]).permute(2, 0, 1)
+        s = q @ k.transpose(-1, -2) * scale + bias
+        if key_mask is not None:
+            s = s.masked_fill(~key_mask.bool()[None, None, :], float("-inf"))
+        return (torch.softmax(s, -1) @ v).transpose(0, 1).reshape(n, H * D)
+
+    @staticmethod
+    def gate(Og, X_rows, Wg, Bg, Wo, Bo):
+        return F.linear(Og * torch.sigmoid(F.linear(X_rows, Wg, Bg)), Wo, Bo)
+
+
+def _apb_inputs():
+    g = torch.Generator().manual_seed(13)
+    M, H, D, Cz = 10, 2, 8, 16
+    C = H * D
+    r = lambda *s, sd=1.0: torch.randn(*s, generator=g) * sd  # noqa: E731
+    w = dict(WQ=r(C, C, sd=C**-0.5), WK=r(C, C, sd=C**-0.5), WV=r(C, C, sd=C**-0.5), W_ln=1 + 0.1 * r(Cz),
+             B_ln=0.1 * r(Cz), Wz=r(Cz, H, sd=Cz**-0.5), Wg=r(C, C, sd=C**-0.5), Bg=0.1 * r(C),
+             Wo=r(C, C, sd=C**-0.5), Bo=0.1 * r(C))
+    km = torch.ones(M, dtype=torch.bool)
+    km[-3:] = False
+    return r(M, C), r(M, M, Cz), w, km, H, D
+
+
+def _apb_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        X, Z, w, km, H, D = _apb_inputs()
+        r0, r1 = tdist.slab(X.shape[0], rank, world)
+        out = tdist.attention_pair_bias_rows(X, Z[r0:r1], {"w": w, "H": H, "D": D}, scale=0.5, W_proj_g=w["Wg"],
+                                             B_proj_g=w["Bg"], W_proj_o=w["Wo"], B_proj_o=w["Bo"], mask=km,
+                                             ops=CpuApbOps)
+        full = tdist.all_gather_rows(out.contiguous(), 0)
+        if rank == 0:
+            q.put(full)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_attention_pair_bias_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_apb_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    X, Z, w, km, H, D = _apb_inputs()
+    ref = oracle.attention_pair_bias_masked(X, w["WQ"], w["WK"], w["WV"], Z, w["W_ln"], w["B_ln"], w["Wz"], None,
+                                            w["Wg"], w["Wo"], H, D, key_mask=km, scale=0.5, B_proj_g=w["Bg"],
+                                            B_proj_o=w["Bo"])
+    assert (full - ref).abs().max().item() < 1e-4

@@ -1,6 +1,6 @@
 """Row-slab sharding on real GPUs (NCCL, 2 ranks): the sharded triangle attention
-(bias all-gather) and triangle multiplicative update (b all-gather, both directions)
-must equal the single-GPU results. Skipped when fewer than 2 GPUs are visible."""
+(bias all-gather), triangle multiplicative update (b all-gather, both directions)
+and pair-bias attention (query rows, no collective) must equal the single-GPU results. Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -21,7 +21,11 @@ def _inputs(dev):
     tm = dict(x=r(1, N, N, C), mask=(torch.rand(1, N, N, generator=g, device=dev) > 0.1),
               w=[1 + 0.1 * r(C), 0.1 * r(C), r(2 * C, C, sd=C**-0.5), r(2 * C, C, sd=C**-0.5), 1 + 0.1 * r(C),
                  0.1 * r(C), r(C, C, sd=C**-0.5), r(C, C, sd=C**-0.5)])
-    return ta, tm
+    M = 512
+    ap = dict(X=r(M, C), Z=r(M, M, C), WQ=r(C, C, sd=C**-0.5), WK=r(C, C, sd=C**-0.5), WV=r(C, C, sd=C**-0.5),
+              W_ln=1 + 0.1 * r(C), B_ln=0.1 * r(C), Wz=r(C, H, sd=C**-0.5), Wg=r(C, C, sd=C**-0.5), Bg=0.1 * r(C),
+              Wo=r(C, C, sd=C**-0.5), Bo=0.1 * r(C), mask=torch.arange(M, device=dev) < M - 40)
+    return ta, tm, ap
 
 
 def _worker(rank, world, port, q):
@@ -35,7 +39,7 @@ def _worker(rank, world, port, q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     try:
-        ta, tm = _inputs(dev)
+        ta, tm, ap = _inputs(dev)
         N = ta["X"].shape[0]
         r0, r1 = tdist.slab(N, rank, world)
         pre = tops.triangle_attn.precompute(ta["W_ln"], ta["B_ln"], ta["WQ"], ta["WK"], ta["WV"], ta["Wz"], None, 4, 32)
@@ -46,7 +50,14 @@ def _worker(rank, world, port, q):
         for direction in ("outgoing", "incoming"):
             o = tdist.triangle_multiplicative_update_rows(tm["x"], prem, direction=direction, mask=tm["mask"])
             res[direction] = tdist.all_gather_rows(o[0].contiguous(), 0).cpu()
+        prea = tops.attn_pair_bias.precompute(ap["WQ"], ap["WK"], ap["WV"], ap["W_ln"], ap["B_ln"], ap["Wz"], None, 4,
+                                              32)
+        gk = dict(W_proj_g=ap["Wg"], B_proj_g=ap["Bg"], W_proj_o=ap["Wo"], B_proj_o=ap["Bo"], mask=ap["mask"])
+        a0, a1 = tdist.slab(ap["X"].shape[0], rank, world)
+        o = tdist.attention_pair_bias_rows(ap["X"], ap["Z"][a0:a1].contiguous(), prea, **gk)
+        res["apb"] = tdist.all_gather_rows(o.contiguous(), 0).cpu()
         if rank == 0:
+            res["ref_apb"] = tops.attn_pair_bias.forward(ap["X"], ap["Z"], prea, **gk).cpu()
             res["ref_tri_attn"] = tops.triangle_attn.forward(ta["X"], pre, mask=ta["mask"], scale=32**-0.5,
                                                              W_proj_g=ta["Wg"], B_proj_g=None, W_proj_o=ta["Wo"],
                                                              B_proj_o=None).cpu()
@@ -74,6 +85,6 @@ def test_sharded_matches_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for key in ("tri_attn", "outgoing", "incoming"):
+    for key in ("tri_attn", "outgoing", "incoming", "apb"):
         d = (res[key].float() - res["ref_" + key].float()).abs().max().item()
         assert d < 1e-2, f"{key}: sharded differs from single-GPU by {d}"

@@ -19,6 +19,9 @@ from .. import _lib
 _P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _lib.register("tops_apb_forward",
               [_I, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P])
+_lib.register("tops_apb_forward_rows",
+              [_I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P,
+               _P, _P])
 
 
 def qkv_rows_from_interleaved(W_QKV, H, D):
@@ -28,13 +31,19 @@ def qkv_rows_from_interleaved(W_QKV, H, D):
     return torch.cat([w[:, :, i, :].reshape(C, H * D).t() for i in range(3)], 0).contiguous()
 
 
-def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, scale=1.0, eps=1e-5, key_mask=None):
+def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, scale=1.0, eps=1e-5, key_mask=None,
+             q0=0):
+    """Pre-gate attention output of query rows [q0, q0 + Z.shape[0]) into ``Og``
+    (Z.shape[0], H*D). X (M, C) holds every token (keys and values need all of
+    them); Z holds the pair rows of those queries, (Mq, M, C_z)."""
     _lib.require_cuda(X, Z, Og)
     M, C = X.shape
-    assert Z.shape == (M, M, Z.shape[-1])
+    Mq = Z.shape[0]
+    assert Z.shape == (Mq, M, Z.shape[-1])
+    assert 0 <= q0 and q0 + Mq <= M
     assert W_combined.shape == (H, Z.shape[-1])
     assert B_const.shape == (H,)
-    assert Og.shape == (M, H * D)
+    assert Og.shape == (Mq, H * D)
     dt = _lib.dtype_code(X.dtype)
     mkp = (M + 7) // 8 * 8
     dev = X.device
@@ -42,7 +51,7 @@ def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, sca
     k = torch.empty(1, H, M, D, dtype=torch.float16, device=dev)
     vt = torch.empty(1, H, D, mkp, dtype=torch.float16, device=dev)
     maskf = torch.empty(1, mkp, dtype=torch.float16, device=dev)
-    bias = torch.empty(H, M, mkp, dtype=torch.float32, device=dev)
+    bias = torch.empty(H, Mq, mkp, dtype=torch.float32, device=dev)
     km = None
     if key_mask is not None:
         km = key_mask.reshape(M)
@@ -54,9 +63,9 @@ def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, sca
     wc = W_combined.float().contiguous()
     sw = sum_W_combined.float().contiguous()
     bc = B_const.float().contiguous()
-    dst = Og if Og.is_contiguous() else torch.empty(M, H * D, dtype=X.dtype, device=dev)
-    _lib.call("tops_apb_forward", dt, M, C, Z.shape[-1], H, D, X.data_ptr(), w_rows.data_ptr(), Z.data_ptr(),
-              wc.data_ptr(), sw.data_ptr(), bc.data_ptr(), _lib.ptr(km), float(scale), float(eps), q.data_ptr(),
+    dst = Og if Og.is_contiguous() else torch.empty(Mq, H * D, dtype=X.dtype, device=dev)
+    _lib.call("tops_apb_forward_rows", dt, M, q0, Mq, C, Z.shape[-1], H, D, X.data_ptr(), w_rows.data_ptr(),
+              Z.data_ptr(), wc.data_ptr(), sw.data_ptr(), bc.data_ptr(), _lib.ptr(km), float(scale), float(eps), q.data_ptr(),
               k.data_ptr(), vt.data_ptr(), maskf.data_ptr(), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(dev))
     if dst is not Og:
         Og.copy_(dst)

@@ -80,14 +80,14 @@ int run_proj(int dtype, int C, int D, bool ln, bool bp, const void* x, const voi
 // ---------------------------------------------------------------------------
 template <typename T, int D, int TR, int TQ, bool BF32>
 int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
-                const void* maskf, const void* bias, void* out, cudaStream_t st) {
+                const void* maskf, const void* bias, void* out, cudaStream_t st, int q_head_rows) {
   using Cfg = AttnCfg<D, TR, TQ, BF32>;
   const CUtensorMapDataType dt = tmap_dtype(dtype);
   const CUtensorMapSwizzle qk_sw = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   CUtensorMap mq, mk, mv, mm, mb;
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nq), static_cast<uint64_t>(R) * H};
-    const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nq) * D * 2};
+    const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(q_head_rows) * D * 2};
     const uint32_t box[3] = {D, 128, 1};
     if (!make_tmap(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
   }
@@ -132,15 +132,19 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
 // TR rows share one bias tile (TR > 1 only pays off when many rows share the bias).
 template <int TR, int TQ, bool BF32 = false>
 int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
-             const void* maskf, const void* bias, void* out, cudaStream_t st) {
+             const void* maskf, const void* bias, void* out, cudaStream_t st, int q_head_rows = 0) {
+  // q_head_rows: rows per head of the Q buffer (Q may be a row window of a longer
+  // [R][H][q_head_rows][D] array, q pointing at its first row); 0 means Nq.
+  if (q_head_rows == 0) q_head_rows = Nq;
+  if (q_head_rows < Nq) return TOPS_ERR_SHAPE;
   if (dtype == TOPS_BF16) {
     if (D == 32)
-      return launch_attn<__nv_bfloat16, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+      return launch_attn<__nv_bfloat16, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
     if (D == 16)
-      return launch_attn<__nv_bfloat16, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+      return launch_attn<__nv_bfloat16, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
   } else if (dtype == TOPS_F16) {
-    if (D == 32) return launch_attn<__half, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
-    if (D == 16) return launch_attn<__half, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st);
+    if (D == 32) return launch_attn<__half, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
+    if (D == 16) return launch_attn<__half, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
   }
   return TOPS_ERR_SHAPE;
 }

@@ -15,8 +15,9 @@
 namespace tops {
 
 struct ZBiasArgs {
-  long long n_tok;      // M * M
-  int M, Mkp;           // query count, padded key stride of the output rows
+  long long n_tok;      // Mq * M
+  int M, Mkp;           // key count, padded key stride of the output rows
+  int Mq;               // query rows in this call (rows of z and of each bias head)
   float eps;
   const float* wc;      // [H][Cz] fp32
   const float* sum_w;   // [H]
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(256) zbias_kernel(const T* __restrict__ z, ZBi
       for (int h = 0; h < H; ++h)
         if (h == sub) bv = fmaf(rstd, dot[h] - mean * sw[h], bc[h]);
       const long long q = tok / a.M, k = tok - q * a.M;
-      a.bias[(static_cast<long long>(sub) * a.M + q) * a.Mkp + k] = bv * 1.4426950408889634f;  // log2 units
+      a.bias[(static_cast<long long>(sub) * a.Mq + q) * a.Mkp + k] = bv * 1.4426950408889634f;  // log2 units
     }
   }
 }

@@ -16,6 +16,12 @@ only where the algorithm exchanges data:
   all-gathered (C*L*L*(P-1)/P elements per rank), then the row-slab contraction
   reads the gathered chunks in place and the output phase runs on the rank's rows.
 
+* attention with pair bias: the bias is per query row, so rank r takes query rows
+  [r*M/P, (r+1)*M/P) with its rows of z (the pair tensor, the only large input)
+  and the whole single sequence X (M x c_s, a few hundred KB), from which it
+  projects K and V for every key itself. No collective: the M*2*H*D K/V elements
+  are cheaper to recompute than to exchange.
+
 The per-rank compute steps are looked up on an ``ops`` object so that the host
 logic (slab partitioning, collective assembly) is testable with gloo on CPU.
 """
@@ -137,3 +143,37 @@ def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-
     y = ops.contract_slab(a, b_chunks, direction, n, L, world)  # (C, n, L)
     out = ops.output_phase(y.reshape(C, n * L), x[0, r0:r1].reshape(n * L, C).contiguous(), pre, eps)
     return out.reshape(1, n, L, C)
+
+
+class ApbKernelOps:
+    """The sm_100a kernels for one rank's query rows of attention with pair bias."""
+
+    @staticmethod
+    def attend_rows(X, Z_rows, pre, q0, scale, eps, key_mask):
+        from .attn_pair_bias.kernel import apb_core
+
+        H, D = pre["H"], pre["D"]
+        w = pre["w_rows"] if pre["w_rows"].dtype == X.dtype else pre["w_rows"].to(X.dtype)
+        Og = torch.empty(Z_rows.shape[0], H * D, device=X.device, dtype=X.dtype)
+        return apb_core(X, w, Z_rows, pre["W_combined"], pre["sum_W_combined"], pre["B_const"], Og, H, D,
+                        scale=scale, eps=eps, key_mask=key_mask, q0=q0)
+
+    @staticmethod
+    def gate(Og, X_rows, W_proj_g, B_proj_g, W_proj_o, B_proj_o):
+        from .triangle_attn.kernel import gate_forward
+
+        return gate_forward(Og, X_rows, W_proj_g, W_proj_o, B_proj_g, B_proj_o)
+
+
+def attention_pair_bias_rows(X, Z_rows, pre, *, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_proj_o, B_proj_o,
+                             mask=None, group=None, ops=ApbKernelOps):
+    """This rank's query rows of attention with pair bias: X (M, c_s) the whole
+    (replicated) single sequence, Z_rows (n, M, C_z) the rank's pair rows
+    z[r0:r1]; returns (n, c_s) = rows [r0, r1) of the unsharded output. No collective."""
+    M = X.shape[0]
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    r0, r1 = slab(M, rank, world)
+    assert Z_rows.shape[:2] == (r1 - r0, M), f"Z_rows must be z[{r0}:{r1}] of shape ({r1 - r0}, {M}, C_z)"
+    Og = ops.attend_rows(X, Z_rows, pre, r0, scale, eps, mask)
+    return ops.gate(Og, X[r0:r1].contiguous(), W_proj_g, B_proj_g, W_proj_o, B_proj_o)
