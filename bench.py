@@ -225,7 +225,39 @@ def other_ops(dev):
     hbm = _peaks()[2]
     out["attention_pair_bias"] = {"config": "M=1024 c_s=C_z=128 bf16, last 64 keys masked", "ms": ms,
                                   "z_gbs": zbytes / ms / 1e6, "frac_of_hbm": zbytes / ms / 1e6 / hbm}
+    del X, Z
+    out["pairformer_pair_update"] = chain_op(dev)
     return out
+
+
+def chain_op(dev, N=2048):
+    """Config 4: tri_mul out -> tri_mul in -> tri_attn start -> tri_attn end (transposed
+    view), x += op(x), ones mask, per-op parameters from seeds 10-13. The fused chain
+    updates x in place (so x drifts over the timed calls; every call does the same work)."""
+    import triangleops_b200 as tops
+
+    def params(seed, kind):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        rn = lambda *s, sd=1.0: (torch.randn(*s, generator=g, device=dev) * sd).to(torch.bfloat16)  # noqa: E731
+        if kind == "tm":
+            return dict(norm_in_weight=1 + 0.1 * rn(C), norm_in_bias=0.1 * rn(C), p_in_weight=rn(2 * C, C, sd=C**-0.5),
+                        g_in_weight=rn(2 * C, C, sd=C**-0.5), norm_out_weight=1 + 0.1 * rn(C),
+                        norm_out_bias=0.1 * rn(C), p_out_weight=rn(C, C, sd=C**-0.5), g_out_weight=rn(C, C, sd=C**-0.5))
+        return dict(W_ln=1 + 0.1 * rn(C), B_ln=0.1 * rn(C), WQ=rn(C, C, sd=C**-0.5), WK=rn(C, C, sd=C**-0.5),
+                    WV=rn(C, C, sd=C**-0.5), W_proj_z=rn(C, H, sd=C**-0.5), B_proj_z=None,
+                    W_proj_g=rn(C, C, sd=C**-0.5), W_proj_o=rn(C, C, sd=C**-0.5), H=H, D=D)
+
+    pre = tops.pairformer.precompute(params(10, "tm"), params(11, "tm"), params(12, "ta"), params(13, "ta"))
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = (torch.randn(N, N, C, generator=g, device=dev)).to(torch.bfloat16)
+    mask = torch.ones(N, N, dtype=torch.bool, device=dev)
+    ms = time_op(lambda: tops.pairformer.pair_update(x, pre, mask=mask), iters=5, warmup=3)
+    ms_unfused = time_op(lambda: tops.pairformer.pair_update_unfused(x, pre, mask=mask), iters=3, warmup=2)
+    flops = 16.2e12
+    _, sus, _, _ = _peaks()
+    return {"config": "Pairformer pair-update chain N=2048 C=128 bf16 (config 4), ones mask", "ms": ms,
+            "tflops": flops / ms / 1e9, "frac_of_sustained_bf16": flops / ms / 1e9 / sus,
+            "ms_per_op_api_composition": ms_unfused}
 
 
 def profile_op(args):

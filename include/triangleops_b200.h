@@ -78,6 +78,18 @@ int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64_t C, int64
                                int apply_ln, const float* ln_w, const float* ln_b, const void* w_qkvz,
                                const float* bz, const uint8_t* mask, float scale, float eps, void* xln_ws,
                                void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws, void* stream);
+
+/* tops_triangle_attn_project for the ending node without a transposed copy: pair
+ * row i of the problem is column i of a square x, token (i, k) at x[(k*N + i)*C]
+ * (x points at column r0 of the full [N][N][C] tensor for a slab of R columns).
+ * mask [R][N] is the transposed mask's rows. N % 8 == 0. The reference's caller
+ * passes X.transpose(0, 1).contiguous() instead (triangle_attn/module.py:53-121 takes
+ * no direction); xln_ws, q/k/vt/maskf/bias are written in the transposed problem's order. */
+int tops_triangle_attn_project_transposed(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
+                                          const void* x, int apply_ln, const float* ln_w, const float* ln_b,
+                                          const void* w_qkvz, const float* bz, const uint8_t* mask, float scale,
+                                          float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws,
+                                          void* maskf_ws, void* bias_ws, void* stream);
 int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_t D, const void* q_ws,
                               const void* k_ws, const void* vt_ws, const void* maskf_ws, const void* bias_ws,
                               void* o_out, void* stream);
@@ -88,6 +100,14 @@ int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_
  *   o, gin, out [T][C]; wg, wo [C][C] (out,in); bg, bo [C] fp32 or NULL. C in {64,128}. */
 int tops_fused_gate_forward(int dtype, int64_t T, int64_t C, const void* o, const void* gin, const void* wg,
                             const void* wo, const float* bg, const float* bo, void* out, void* stream);
+
+/* tops_fused_gate_forward plus the Pairformer residual (no counterpart in the reference,
+ * whose caller adds x + op(x) in torch): out[r(t)] = residual[r(t)] + gate result of token
+ * t, where r(t) = t, or, with trans_n = n > 0, r(i*n + k) = k*n + i (the ending-node
+ * result stored back in the untransposed layout). residual may be NULL or alias out. */
+int tops_fused_gate_residual(int dtype, int64_t T, int64_t C, const void* o, const void* gin, const void* wg,
+                             const void* wo, const float* bg, const float* bo, const void* residual, void* out,
+                             int64_t trans_n, void* stream);
 
 /* ---------------------------------------------------------------------------
  * triangle multiplicative update
@@ -117,6 +137,13 @@ int tops_trimul_contract_slab(int dtype, int direction, int64_t nb, int64_t Mi, 
  *   out [M][C]; M % 8 == 0. */
 int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const void* y, const void* x, const void* w_out,
                              const float* sum_out, const float* b_out, float eps, void* out, void* stream);
+
+/* tops_trimul_output_phase with the Pairformer residual added in the epilogue (no
+ * counterpart in the reference): out = residual + update; residual may alias out and x
+ * (the in-place x += triangle_multiplicative_update(x)). */
+int tops_trimul_output_phase_residual(int dtype, int64_t M, int64_t C, const void* y, const void* x,
+                                      const void* w_out, const float* sum_out, const float* b_out, float eps,
+                                      const void* residual, void* out, void* stream);
 /* The whole op (triangle_mul/module.py:55-88 forward): input phase -> contraction ->
  * output phase. x [B][L][L][C] (L % 8 == 0), mask [B*L*L] int8 or NULL,
  * ab_ws [2C][B*L*L], y_ws [C][B*L*L], out [B][L][L][C]. */

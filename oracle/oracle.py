@@ -13,6 +13,9 @@ implementation of one op (youngchan2/TriangleOps ``benchmarks/references.py``):
 * :func:`triangle_multiplicative_update`  <- ``references.py:208-221``
 * :func:`attention_pair_bias`             <- ``references.py:143-171``
 * :func:`attention_pair_bias_masked`      <- ``references.py:224-277`` with ``b_q=0``, no qk-norm
+* :func:`pair_update`                     <- the four triangle ops chained with residual adds
+  (out, in, starting, ending = transposed view), composed from
+  the functions above
 
 plus the LN-affine fold of ``triangle_ops/_common/ln_absorption.py:28-63``
 (:func:`absorb_ln`, :func:`absorb_ln_matmul`).
@@ -224,3 +227,37 @@ def attention_pair_bias_masked(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z,
     qk-norm): masked keys get -inf before the softmax (``references.py:273-274``)."""
     return _apb(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z, W_proj_g, B_proj_g, W_proj_o, B_proj_o, H, D,
                 scale, eps, key_mask, io_round)
+
+
+# --------------------------------------------------------------------------- #
+# Pairformer pair-update chain (composition of the functions above)
+# --------------------------------------------------------------------------- #
+def pair_update(x, *, tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end, mask=None, scale=None, eps=1e-5,
+                io_round=None, stages=("tri_mul_out", "tri_mul_in", "tri_attn_start", "tri_attn_end")):
+    """x (N, N, C) -> x + the four triangle updates in order, fp32 CPU:
+    x += trimul_out(x); x += trimul_in(x); x += tri_attn(x); x += tri_attn(x^T)^T with
+    mask^T (ending node as the transposed view). ``tri_mul_*``: the eight trimul
+    weights; ``tri_attn_*``: W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g,
+    W_proj_o, H, D. ``stages`` selects a sub-sequence. ``io_round`` rounds what a chain in the IO dtype stores: each op's
+    intermediates (the ops' own ``io_round``), each op's output and x after every add."""
+    (x,) = _f32(x)
+    r = io_round
+    N = x.shape[0]
+    m = None if mask is None else mask.detach().to("cpu").reshape(N, N)
+    m3 = None if m is None else m.reshape(1, N, N)
+    for w, direction, name in ((tri_mul_out, "outgoing", "tri_mul_out"), (tri_mul_in, "incoming", "tri_mul_in")):
+        if name not in stages:
+            continue
+        x = _rt(x + _rt(triangle_multiplicative_update(x[None], direction=direction, mask=m3, eps=eps, io_round=r,
+                                                       **w)[0], r), r)
+    for w, ending, name in ((tri_attn_start, False, "tri_attn_start"), (tri_attn_end, True, "tri_attn_end")):
+        if name not in stages:
+            continue
+        sc = w["D"] ** -0.5 if scale is None else scale
+        src = x.transpose(0, 1) if ending else x
+        mm = None if m is None else (m.t() if ending else m)
+        o = triangle_attention(src, w["W_ln"], w["B_ln"], w["WQ"], w["WK"], w["WV"], w["W_proj_z"], w["B_proj_z"],
+                               w["W_proj_g"], None, w["W_proj_o"], None, w["H"], w["D"], scale=sc, eps=eps, mask=mm,
+                               io_round=r)
+        x = _rt(x + _rt(o.transpose(0, 1) if ending else o, r), r)
+    return x

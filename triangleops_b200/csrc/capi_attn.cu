@@ -44,12 +44,20 @@ template <typename T, int C, int D, bool LN, bool BP>
 int launch_proj(int dtype, const void* x, const void* w, const ProjArgs& args, cudaStream_t st) {
   using Cfg = ProjCfg<C, BP>;
   CUtensorMap mx, mw;
-  if (!map_rows(&mx, dtype, x, args.T, C, 128)) return TOPS_ERR_TMAP;
+  if (args.trans) {
+    // token (i, k) at x[k * Nk + i]: dims {C, i, k}, one box = 128 positions k of one column i
+    const uint64_t dims[3] = {static_cast<uint64_t>(C), static_cast<uint64_t>(args.R), static_cast<uint64_t>(args.Nk)};
+    const uint64_t str[2] = {static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(args.Nk) * C * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    if (!make_tmap(&mx, tmap_dtype(dtype), 3, x, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+  } else if (!map_rows(&mx, dtype, x, args.T, C, 128)) {
+    return TOPS_ERR_TMAP;
+  }
   if (!map_rows(&mw, dtype, w, Cfg::NOUT, C, Cfg::WBOX)) return TOPS_ERR_TMAP;
   const size_t smem = sizeof(ProjSmem<C, BP>) + 1024;
   auto kern = proj_kernel<T, C, D, LN, BP>;
   set_smem(kern, smem);
-  const int tiles = (args.T + 127) / 128;
+  const int tiles = args.trans ? args.R * ((args.Nk + 127) / 128) : (args.T + 127) / 128;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, 384, smem, st>>>(mx, mw, args);
   return launch_status();
@@ -154,13 +162,13 @@ int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void
 // ---------------------------------------------------------------------------
 template <typename T, int C>
 int launch_gate(int dtype, int64_t T_, const void* o, const void* gin, const void* wg, const void* wo, const float* bg,
-                const float* bo, void* out, cudaStream_t st) {
+                const float* bo, void* out, cudaStream_t st, const void* residual, int trans_n) {
   CUtensorMap mg, mo, mwg, mwo;
   if (!map_rows(&mg, dtype, gin, T_, C, 128)) return TOPS_ERR_TMAP;
   if (!map_rows(&mo, dtype, o, T_, C, 128)) return TOPS_ERR_TMAP;
   if (!map_rows(&mwg, dtype, wg, C, C, C)) return TOPS_ERR_TMAP;
   if (!map_rows(&mwo, dtype, wo, C, C, C)) return TOPS_ERR_TMAP;
-  GateArgs args{static_cast<int>(T_), bg, bo, out};
+  GateArgs args{static_cast<int>(T_), bg, bo, out, residual, trans_n};
   const size_t smem = sizeof(GateSmem<C>) + 1024;
   auto kern = gate_kernel<T, C>;
   set_smem(kern, smem);
@@ -171,13 +179,14 @@ int launch_gate(int dtype, int64_t T_, const void* o, const void* gin, const voi
 }
 
 int run_gate(int dtype, int64_t T_, int64_t C, const void* o, const void* gin, const void* wg, const void* wo,
-             const float* bg, const float* bo, void* out, cudaStream_t st) {
+             const float* bg, const float* bo, void* out, cudaStream_t st, const void* residual = nullptr,
+             int trans_n = 0) {
   if (dtype == TOPS_BF16) {
-    if (C == 128) return launch_gate<__nv_bfloat16, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
-    if (C == 64) return launch_gate<__nv_bfloat16, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+    if (C == 128) return launch_gate<__nv_bfloat16, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st, residual, trans_n);
+    if (C == 64) return launch_gate<__nv_bfloat16, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st, residual, trans_n);
   } else if (dtype == TOPS_F16) {
-    if (C == 128) return launch_gate<__half, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
-    if (C == 64) return launch_gate<__half, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st);
+    if (C == 128) return launch_gate<__half, 128>(dtype, T_, o, gin, wg, wo, bg, bo, out, st, residual, trans_n);
+    if (C == 64) return launch_gate<__half, 64>(dtype, T_, o, gin, wg, wo, bg, bo, out, st, residual, trans_n);
   }
   return TOPS_ERR_SHAPE;
 }
@@ -190,11 +199,10 @@ inline bool attn_shape_ok(int64_t C, int64_t H, int64_t D) {
 
 using namespace tops;
 
-extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
-                                          const void* x, int apply_ln, const float* ln_w, const float* ln_b,
-                                          const void* w_qkvz, const float* bz, const uint8_t* mask, float scale,
-                                          float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws,
-                                          void* maskf_ws, void* bias_ws, void* stream) {
+static int project_impl(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D, const void* x, int apply_ln,
+                        const float* ln_w, const float* ln_b, const void* w_qkvz, const float* bz, const uint8_t* mask,
+                        float scale, float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws,
+                        void* bias_ws, void* stream, int trans) {
   if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
   if (N <= 0 || R <= 0 || R > N || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
   if (R * N >= (int64_t(1) << 31)) return TOPS_ERR_SHAPE;
@@ -206,9 +214,29 @@ extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64
   const int n = static_cast<int>(N), r = static_cast<int>(R);
   const int nkp = (n + 7) & ~7;
   ProjArgs pa{r * n, n, r, nkp, scale * kLog2e, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
-              q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
+              q_ws, k_ws, vt_ws, maskf_ws, bias_ws, trans};
   return run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa,
                   static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
+                                          const void* x, int apply_ln, const float* ln_w, const float* ln_b,
+                                          const void* w_qkvz, const float* bz, const uint8_t* mask, float scale,
+                                          float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws,
+                                          void* maskf_ws, void* bias_ws, void* stream) {
+  return project_impl(dtype, R, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps, xln_ws, q_ws, k_ws,
+                      vt_ws, maskf_ws, bias_ws, stream, 0);
+}
+
+extern "C" int tops_triangle_attn_project_transposed(int dtype, int64_t R, int64_t N, int64_t C, int64_t H,
+                                                     int64_t D, const void* x, int apply_ln, const float* ln_w,
+                                                     const float* ln_b, const void* w_qkvz, const float* bz,
+                                                     const uint8_t* mask, float scale, float eps, void* xln_ws,
+                                                     void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws,
+                                                     void* bias_ws, void* stream) {
+  if (N % 8 != 0) return TOPS_ERR_ALIGN;  // the column stride N*C*2 bytes must be a multiple of 16
+  return project_impl(dtype, R, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps, xln_ws, q_ws, k_ws,
+                      vt_ws, maskf_ws, bias_ws, stream, 1);
 }
 
 extern "C" int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_t D, const void* q_ws,
@@ -244,6 +272,20 @@ extern "C" int tops_fused_gate_forward(int dtype, int64_t T_, int64_t C, const v
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tops_fused_gate_residual(int dtype, int64_t T_, int64_t C, const void* o, const void* gin,
+                                        const void* wg, const void* wo, const float* bg, const float* bo,
+                                        const void* residual, void* out, int64_t trans_n, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (T_ <= 0 || T_ >= (int64_t(1) << 31) || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  if (trans_n < 0 || (trans_n > 0 && T_ % trans_n != 0)) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {o, gin, wg, wo, out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  if (residual != nullptr && !aligned16(residual)) return TOPS_ERR_ALIGN;
+  return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream), residual,
+                  static_cast<int>(trans_n));
 }
 
 #ifdef TOPS_TRACE

@@ -172,6 +172,19 @@ extern "C" int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const v
   return run_trimul_out(dtype, static_cast<int>(C), y, x, w_out, args, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int tops_trimul_output_phase_residual(int dtype, int64_t M, int64_t C, const void* y, const void* x,
+                                                 const void* w_out, const float* sum_out, const float* b_out,
+                                                 float eps, const void* residual, void* out, void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (M <= 0 || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  if (M % 8 != 0) return TOPS_ERR_ALIGN;
+  const void* ptrs[] = {y, x, w_out, sum_out, b_out, residual, out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  LnGateArgs args{M, eps, sum_out, b_out, nullptr, out, residual};
+  return run_trimul_out(dtype, static_cast<int>(C), y, x, w_out, args, static_cast<cudaStream_t>(stream));
+}
+
 // The whole op: input phase -> contraction -> output phase on one stream.
 // ab_ws: [2C][B*L*L] workspace, y_ws: [C][B*L*L] workspace.
 extern "C" int tops_trimul_forward(int dtype, int direction, int64_t B, int64_t L, int64_t C, const void* x,

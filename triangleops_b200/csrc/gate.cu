@@ -9,7 +9,8 @@
 // gate, multiplies the attention output O (read from the same shared-memory stage),
 // rounds to the IO dtype — the rounding point of the reference — and writes the
 // product over the gin tile (gin is dead once MMA1 completes); MMA2 acc2 = that
-// product times Wo^T; the warpgroup adds bo and stores. Two warpgroups alternate
+// product times Wo^T; the warpgroup adds bo (and optionally a residual: the
+// Pairformer update x += op(x), in place) and stores, optionally transposed. Two warpgroups alternate
 // tiles, each with its own TMEM accumulator pair, and MMA1 of the next tile is
 // issued before MMA2 of the current one so the tensor core never waits on a gate.
 #include "sm100.cuh"
@@ -41,6 +42,9 @@ struct GateArgs {
   const float* bg;  // [C] or nullptr
   const float* bo;  // [C] or nullptr
   void* out;        // [T][C]
+  const void* residual;  // nullptr, or added to the result; same indexing as out (may alias out)
+  int trans_n;      // 0: token t -> out row t. n > 0: token t = i*n + k -> out row k*n + i
+                    // (the ending-node result written back in the untransposed pair layout)
 };
 
 template <typename T, int C>
@@ -173,12 +177,30 @@ __global__ void __launch_bounds__(384, 1)
       if (!mbar_wait(&sm.acc2_full[s], (it >> 1) & 1, abort, 307)) break;
       tc_fence_after();
       const long long tok = static_cast<long long>(tile) * 128 + row;
-      T* dst = static_cast<T*>(a.out) + tok * C;
+      long long orow = tok;
+      if (a.trans_n > 0) {
+        const long long i = tok / a.trans_n;
+        orow = (tok - i * a.trans_n) * a.trans_n + i;
+      }
+      T* dst = static_cast<T*>(a.out) + orow * C;
+      const T* res = a.residual != nullptr ? static_cast<const T*>(a.residual) + orow * C : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < C; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(acc2 + c0, r);
         if (tok < a.T) {
+          uint32_t rs[16];
+          if (res != nullptr) {
+            const uint4* r4 = reinterpret_cast<const uint4*>(res + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = r4[q];
+              rs[4 * q] = u.x;
+              rs[4 * q + 1] = u.y;
+              rs[4 * q + 2] = u.z;
+              rs[4 * q + 3] = u.w;
+            }
+          }
           uint32_t p[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -186,6 +208,10 @@ __global__ void __launch_bounds__(384, 1)
             if (a.bo != nullptr) {
               v0 += __ldg(a.bo + c0 + 2 * e);
               v1 += __ldg(a.bo + c0 + 2 * e + 1);
+            }
+            if (res != nullptr) {
+              v0 += E::lo(rs[e]);
+              v1 += E::hi(rs[e]);
             }
             p[e] = E::pack2(v0, v1);
           }

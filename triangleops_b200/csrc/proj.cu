@@ -53,7 +53,27 @@ struct ProjArgs {
   void* vt;
   void* maskf;
   void* bp;
+  int trans;           // 1: token (i, k) is x[k][i] of a square [Nk][Nk] pair array (ending node)
 };
+
+// Token tiles. Row-major input: 128 consecutive tokens of the flattened stream.
+// Transposed input: tiles never straddle a row i, so that one 3-D TMA box (128
+// positions k of column i, stride Nk*C) fills the tile; the last tile of a row is ragged.
+__device__ __forceinline__ int proj_tiles(const ProjArgs& a) {
+  return a.trans ? a.R * ((a.Nk + 127) / 128) : (a.T + 127) / 128;
+}
+__device__ __forceinline__ long long proj_token(const ProjArgs& a, int tile, int row, bool& valid) {
+  if (a.trans) {
+    const int tpr = (a.Nk + 127) / 128;
+    const int i = tile / tpr;
+    const int k = (tile - i * tpr) * 128 + row;
+    valid = k < a.Nk;
+    return static_cast<long long>(i) * a.Nk + k;
+  }
+  const long long tok = static_cast<long long>(tile) * 128 + row;
+  valid = tok < a.T;
+  return tok;
+}
 
 template <int C, bool HAS_BP>
 struct ProjSmem {
@@ -79,7 +99,7 @@ __global__ void __launch_bounds__(384, 1)
   extern __shared__ uint8_t smem_raw[];
   auto& sm = *reinterpret_cast<ProjSmem<C, HAS_BP>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tiles = (a.T + 127) / 128;
+  const int n_tiles = proj_tiles(a);
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_w, 1);
@@ -114,8 +134,15 @@ __global__ void __launch_bounds__(384, 1)
         const int s = it & 1;
         if (!mbar_wait(&sm.bar_x_empty[s], ((it >> 1) & 1) ^ 1, abort, 101)) break;
         mbar_expect_tx(&sm.bar_x_full[s], Cfg::XSTAGE);
-        for (int ka = 0; ka < Cfg::KATOMS; ++ka)
-          tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.bar_x_full[s], ka * 64, tile * 128);
+        if (a.trans) {
+          const int tpr = (a.Nk + 127) / 128;
+          const int i = tile / tpr, k0 = (tile - i * tpr) * 128;
+          for (int ka = 0; ka < Cfg::KATOMS; ++ka)
+            tma_load_3d(sm.x[s] + ka * 16384, &map_x, &sm.bar_x_full[s], ka * 64, i, k0);
+        } else {
+          for (int ka = 0; ka < Cfg::KATOMS; ++ka)
+            tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.bar_x_full[s], ka * 64, tile * 128);
+        }
       }
     }
   } else if (warp == 1) {
@@ -181,8 +208,9 @@ __global__ void __launch_bounds__(384, 1)
           var = fmaf(d0, d0, fmaf(d1, d1, var));
         }
         const float rstd = rsqrtf(var * (1.0f / C) + a.eps);
-        const long long tok = static_cast<long long>(tile) * 128 + row;
-        T* xo = a.xln_out != nullptr && tok < a.T ? static_cast<T*>(a.xln_out) + tok * C : nullptr;
+        bool tvalid;
+        const long long tok = proj_token(a, tile, row, tvalid);
+        T* xo = a.xln_out != nullptr && tvalid ? static_cast<T*>(a.xln_out) + tok * C : nullptr;
 #pragma unroll
         for (int ka = 0; ka < Cfg::KATOMS; ++ka)
 #pragma unroll
@@ -217,8 +245,8 @@ __global__ void __launch_bounds__(384, 1)
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       if (!mbar_wait(&sm.bar_acc_full, it & 1, abort, 106)) break;
       tc_fence_after();
-      const long long tok = static_cast<long long>(tile) * 128 + row;
-      const bool valid = tok < a.T;
+      bool valid;
+      const long long tok = proj_token(a, tile, row, valid);
       const int ri = valid ? static_cast<int>(tok / a.Nk) : 0;
       const int kpos = valid ? static_cast<int>(tok - static_cast<long long>(ri) * a.Nk) : 0;
       float mval = 1.0f;

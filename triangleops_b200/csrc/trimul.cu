@@ -23,6 +23,7 @@ struct LnGateArgs {
   const float* b_const;  // [NOUT] folded biases (fp32)
   const uint8_t* mask;   // [M] int8 multiplier (input phase only; nullptr = none)
   void* out;
+  const void* residual;  // output phase: nullptr, or [M][C] added to the result (may alias out)
 };
 
 // LayerNorm statistics of a 128 x C row-major (K-major, SW128) staged tile row.
@@ -516,12 +517,25 @@ __global__ void __launch_bounds__(384, 1)
       tc_fence_after();
       const long long m = tile * 128 + row;
       T* dst = static_cast<T*>(a.out) + m * C;
+      const T* res = a.residual != nullptr ? static_cast<const T*>(a.residual) + m * C : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < C; c0 += 32) {
         uint32_t p[32], g[32];
         tmem_ld32(lane_addr + s * 256 + c0, p);
         tmem_ld32(lane_addr + s * 256 + C + c0, g);
         if (m < a.M) {
+          uint32_t rs[16];
+          if (res != nullptr) {
+            const uint4* r4 = reinterpret_cast<const uint4*>(res + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 u = r4[q];
+              rs[4 * q] = u.x;
+              rs[4 * q + 1] = u.y;
+              rs[4 * q + 2] = u.z;
+              rs[4 * q + 3] = u.w;
+            }
+          }
           uint32_t o[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -533,6 +547,10 @@ __global__ void __launch_bounds__(384, 1)
               const float gv =
                   fmaf(rx, __uint_as_float(g[2 * e + h]) - mx * __ldg(a.sum_w + C + c), __ldg(a.b_const + C + c));
               v[h] = sigmoid_fast(gv) * pv;
+            }
+            if (res != nullptr) {
+              v[0] += E::lo(rs[e]);
+              v[1] += E::hi(rs[e]);
             }
             o[e] = E::pack2(v[0], v[1]);
           }

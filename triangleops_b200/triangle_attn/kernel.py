@@ -21,6 +21,7 @@ _P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _lib.register("tops_triangle_attn_forward",
               [_I, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P, _P])
 _lib.register("tops_fused_gate_forward", [_I, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P])
+_lib.register("tops_fused_gate_residual", [_I, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P])
 
 
 def _mask_u8(mask, shape):
@@ -97,8 +98,13 @@ def triangle_attn_forward(X_ln, WQ_c, WKV_c, WZ_c, BZ, out, scale=1.0, mask=None
     return out
 
 
-def gate_forward(o, gin, WG, WO, BG=None, BO=None, out=None):
-    """out = (o * sigmoid(gin WG^T + BG)) WO^T + BO over (T, C) token rows."""
+def gate_forward(o, gin, WG, WO, BG=None, BO=None, out=None, residual=None, trans_n=0):
+    """out = (o * sigmoid(gin WG^T + BG)) WO^T + BO over (T, C) token rows.
+
+    ``residual`` (same layout as ``out``, may be ``out`` itself) is added in the
+    epilogue. ``trans_n`` = n > 0 writes token t = i*n + k to out row k*n + i, i.e.
+    the result of an ending-node (transposed) problem lands in the untransposed
+    pair layout."""
     _lib.require_cuda(o, gin, WG, WO)
     dt = _lib.dtype_code(gin.dtype)
     C = gin.shape[-1]
@@ -114,8 +120,16 @@ def gate_forward(o, gin, WG, WO, BG=None, BO=None, out=None):
     bo = None if BO is None else BO.float().contiguous()
     if out is None:
         out = torch.empty(T, C, dtype=gin.dtype, device=gin.device)
-    _lib.call("tops_fused_gate_forward", dt, T, C, o2.data_ptr(), g2.data_ptr(), wg.data_ptr(), wo.data_ptr(),
-              _lib.ptr(bg), _lib.ptr(bo), out.data_ptr(), _lib.stream_ptr(gin.device))
+    if residual is None and trans_n == 0:
+        _lib.call("tops_fused_gate_forward", dt, T, C, o2.data_ptr(), g2.data_ptr(), wg.data_ptr(), wo.data_ptr(),
+                  _lib.ptr(bg), _lib.ptr(bo), out.data_ptr(), _lib.stream_ptr(gin.device))
+        return out
+    assert out.is_contiguous() and out.numel() == T * C
+    assert residual is None or (residual.is_contiguous() and residual.numel() == T * C
+                                and residual.dtype == gin.dtype)
+    _lib.call("tops_fused_gate_residual", dt, T, C, o2.data_ptr(), g2.data_ptr(), wg.data_ptr(), wo.data_ptr(),
+              _lib.ptr(bg), _lib.ptr(bo), _lib.ptr(residual), out.data_ptr(), int(trans_n),
+              _lib.stream_ptr(gin.device))
     return out
 
 
@@ -128,7 +142,16 @@ def fused_gate_forward(o_attn, qx_ln, WG, WO):
 
 _lib.register("tops_triangle_attn_project",
               [_I, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P])
+_lib.register("tops_triangle_attn_project_transposed",
+              [_I, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, _P])
 _lib.register("tops_triangle_attn_attend", [_I, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P])
+
+
+def is_transposed_rows(X_rows):
+    """True for rows of the transposed view of a contiguous square (N, N, C) pair
+    tensor: strides (C, N*C, 1) with more than one row."""
+    R, N, C = X_rows.shape
+    return R > 1 and N > 1 and X_rows.stride() == (C, N * C, 1)
 
 
 def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, scale=1.0, eps=1e-5):
@@ -136,10 +159,17 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
 
     Returns dict(q, k, vt, maskf, bias, xln): bias holds this slab's rows of the
     shared bias, (H, R, Np) f16 in log2 units; the others are row-local attention
-    operands (vt and maskf f16)."""
+    operands (vt and maskf f16). X_rows may be rows of a transposed view
+    (``X.transpose(0, 1)[r0:r1]`` of a contiguous square X, the ending node): the
+    projection then reads X column-wise through a 3-D tensor map, without a copy."""
     _lib.require_cuda(X_rows)
     R, N2, C = X_rows.shape
     assert N2 == N
+    if is_transposed_rows(X_rows) and N % 8 == 0:
+        entry = "tops_triangle_attn_project_transposed"
+    else:
+        entry = "tops_triangle_attn_project"
+        X_rows = X_rows.contiguous()
     dt = _lib.dtype_code(X_rows.dtype)
     nkp = (N + 7) // 8 * 8
     dev, dty = X_rows.device, X_rows.dtype
@@ -149,9 +179,8 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
               maskf=torch.empty(R, nkp, dtype=torch.float16, device=dev),
               bias=torch.empty(H, R, nkp, dtype=torch.float16, device=dev),
               xln=torch.empty(R, N, C, dtype=dty, device=dev))
-    X_rows = X_rows.contiguous()
     m = _mask_u8(mask_rows, (R, N))
-    _lib.call("tops_triangle_attn_project", dt, R, N, C, H, D, X_rows.data_ptr(), 1, ln_w.data_ptr(),
+    _lib.call(entry, dt, R, N, C, H, D, X_rows.data_ptr(), 1, ln_w.data_ptr(),
               ln_b.data_ptr(), w_qkvz.data_ptr(), bz.data_ptr(), _lib.ptr(m), float(scale), float(eps),
               ws["xln"].data_ptr(), ws["q"].data_ptr(), ws["k"].data_ptr(), ws["vt"].data_ptr(),
               ws["maskf"].data_ptr(), ws["bias"].data_ptr(), _lib.stream_ptr(dev))

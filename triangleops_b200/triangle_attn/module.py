@@ -14,7 +14,7 @@ import torch
 
 from .. import _f32
 from .._common.layouts import interleave_kv, qkv_rows
-from .kernel import gate_forward, triangle_attn_fused_forward
+from .kernel import attend_rows, gate_forward, is_transposed_rows, project_rows, triangle_attn_fused_forward
 
 
 def precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D):
@@ -75,8 +75,14 @@ def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_pro
     w = pre["W_qkvz"]
     if w.dtype != X.dtype:
         w = w.to(X.dtype)
-    O, X_ln = triangle_attn_fused_forward(X, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, mask=mask,
-                                          scale=scale, eps=eps)
+    if is_transposed_rows(X) and N % 8 == 0:
+        # ending node passed as X.transpose(0, 1): read column-wise in place, no copy
+        ws = project_rows(X, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=N, mask_rows=mask, scale=scale,
+                          eps=eps)
+        O, X_ln = attend_rows(ws, ws["bias"], H, D), ws["xln"]
+    else:
+        O, X_ln = triangle_attn_fused_forward(X, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, mask=mask,
+                                              scale=scale, eps=eps)
     if mask is not None:
         WV = w[2 * H * D:3 * H * D].t()
         _fix_fully_masked_rows(O, X_ln, WV, mask, H, D)

@@ -19,6 +19,7 @@ _lib.register("tops_trimul_input_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F
 _lib.register("tops_trimul_contract", [_I, _I, _I64, _I64, _P, _P, _P, _P])
 _lib.register("tops_trimul_contract_slab", [_I, _I, _I64, _I64, _I64, _I64, _P, _P, _P, _P])
 _lib.register("tops_trimul_output_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P])
+_lib.register("tops_trimul_output_phase_residual", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P, _P])
 _lib.register("tops_trimul_forward",
               [_I, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _P])
 
@@ -161,3 +162,31 @@ def output_phase_tokens(y_dmajor, x_tokens, pre, eps=1e-5):
               pre["sum_out"].data_ptr(), pre["b_out"].data_ptr(), float(eps), out.data_ptr(),
               _lib.stream_ptr(x_tokens.device))
     return out
+
+
+def residual_update(x, pre, direction, mask=None, eps=1e-5, ab_ws=None, y_ws=None):
+    """x += triangle_multiplicative_update(x), in place (the Pairformer residual
+    update): input phase -> contraction -> output phase with the residual added in
+    its epilogue. x (B, L, L, C) contiguous, L % 8 == 0."""
+    code = direction_code(direction)
+    _lib.require_cuda(x)
+    assert x.is_contiguous(), "the in-place update needs a contiguous x"
+    B, L, _, C = x.shape
+    M = B * L * L
+    dt = _lib.dtype_code(x.dtype)
+    if ab_ws is None:
+        ab_ws = torch.empty(2 * C, M, device=x.device, dtype=x.dtype)
+    if y_ws is None:
+        y_ws = torch.empty(C, M, device=x.device, dtype=x.dtype)
+    w_in, w_out = pre["w_in"], pre["w_out"]
+    if w_in.dtype != x.dtype:
+        w_in, w_out = w_in.to(x.dtype), w_out.to(x.dtype)
+    m = mask_u8(mask, M)
+    st = _lib.stream_ptr(x.device)
+    _lib.call("tops_trimul_input_phase", dt, M, C, x.data_ptr(), _lib.ptr(m), w_in.data_ptr(),
+              pre["sum_in"].data_ptr(), pre["b_in"].data_ptr(), float(eps), ab_ws.data_ptr(), st)
+    _lib.call("tops_trimul_contract", dt, code, C * B, L, ab_ws.data_ptr(), ab_ws[C:].data_ptr(), y_ws.data_ptr(),
+              st)
+    _lib.call("tops_trimul_output_phase_residual", dt, M, C, y_ws.data_ptr(), x.data_ptr(), w_out.data_ptr(),
+              pre["sum_out"].data_ptr(), pre["b_out"].data_ptr(), float(eps), x.data_ptr(), x.data_ptr(), st)
+    return x
