@@ -14,14 +14,19 @@
 // column D. Masked keys therefore contribute to neither O nor l (the reference's
 // -1e9 additive mask gives the same result for any row with >= 1 unmasked key).
 //
+// Bias without per-element work (f16 bias, triangle attention): the tensor core adds
+// it — S = bias x I + Q K^T, with I the 64 x 64 identity in shared memory (products
+// and sums exact in the fp32 accumulator) — so the softmax reads S ready-biased.
+// The fp32 bias of the pair-bias attention is added by the softmax.
+//
 // Cost model (measured on B200): a tcgen05.mma with M=128, K=16 keeps its issuing
 // thread busy for ~140 cycles whatever N is (up to N=128), while the tensor core
 // itself can absorb a new small MMA every ~50 cycles when several warps issue. At
 // D=32 the work per key block is many small MMAs (QK^T: D/16, PV: BK/16), so each
 // tile has its OWN issuing warp: the tiles' MMA streams overlap in the tensor core.
 //
-// Per CTA: w0 TMA producer (K, V^T, mask row, bias tile per 64-key block into a ring
-// of stages), w(1+t) MMA issuer of tile t, one softmax warpgroup per tile (one TMEM
+// Per CTA: w0 TMA producer (per 64-key block: bias and K tiles into ring A, V^T and
+// mask rows into ring B), w(1+t) MMA issuer of tile t, one softmax warpgroup per tile (one TMEM
 // lane = one query row per thread). TMEM per tile: S (64 fp32 columns), P (32
 // columns of packed f16 pairs, the A operand of PV) and O (D+16 columns). The
 // softmax releases S as soon as it has loaded it, so QK^T(j+1) runs while the
@@ -32,10 +37,23 @@
 // max grows by more than 2^8). The per-element work runs on f16 pairs: S + bias is
 // rounded to f16 (relative error 2^-11, well below the 2^-8 rounding the 16-bit Q
 // and K already put into S), the row max is a pairwise tree, and
-// P = ex2.approx.f16x2(x - m); V^T and the mask row are f16 for the PV MMA.
+// P = 2^(x - m), 3/5 of the pairs on the MUFU (ex2.approx.f16x2, which issues twice
+// on the XU pipe) and 2/5 by a polynomial on the FMA pipe (ex2_poly_f16x2), so that
+// neither pipe alone bounds the step; V^T and the mask row are f16 for the PV MMA.
 #include "sm100.cuh"
 
 namespace tops {
+
+#ifndef TOPS_POLY_EXP
+#define TOPS_POLY_EXP 1
+#endif
+constexpr bool kPolyExp = TOPS_POLY_EXP != 0;
+#ifndef TOPS_POLY_PICK
+#define TOPS_POLY_PICK(c) ((c) % 5 == 1 || (c) % 5 == 3)  // pairs whose 2^x takes the polynomial
+#endif
+#ifndef TOPS_ATTN_SMEM_KB
+#define TOPS_ATTN_SMEM_KB 200  // operand budget (Q tiles + stages); the B200 allows 227 KB per CTA
+#endif
 
 // Optional phase timers (build with -DTOPS_TRACE): per-role cycle sums, read back
 // with tops_attn_trace(). Compiled out of the library by default.
@@ -63,18 +81,25 @@ struct AttnCfg {
   static constexpr int K_BYTES = BK * D * 2;
   static constexpr int V_BYTES = NPV * 128;     // NPV rows x 64 keys (128 B, SW128)
   static constexpr int B_BYTES = 128 * BK * (BF32 ? 4 : 2);  // bias tile (SW128; fp32: two 32-key boxes)
-  static constexpr int STAGE = TQ * B_BYTES + TR * (K_BYTES + V_BYTES);
-  static constexpr int STAGE_TX = TQ * B_BYTES + TR * (K_BYTES + D * 128 + 128);
-  static constexpr int NS_FIT = (200 * 1024 - NT * Q_BYTES) / STAGE;
-  static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;  // pipeline stages
+  // Two operand rings, released at different times: ring A (bias tiles + K tiles) is
+  // free once QK^T has run and the softmax has read the bias, ring B (V^T with its
+  // mask row) once PV has run — a block later. Separate rings let the next blocks'
+  // K and bias stream in without waiting for the slower PV release.
+  static constexpr int A_BYTES = TQ * B_BYTES + TR * K_BYTES;
+  static constexpr int VB_BYTES = TR * V_BYTES;
+  static constexpr int VB_TX = TR * (D * 128 + 128);
+  static constexpr int BUDGET = TOPS_ATTN_SMEM_KB * 1024 - NT * Q_BYTES - (BF32 ? 1024 : BK * 128);
+  static constexpr int NB = 4;
+  static constexpr int NA_FIT = (BUDGET - NB * VB_BYTES) / A_BYTES;
+  static constexpr int NA = NA_FIT > 4 ? 4 : NA_FIT;
   static constexpr uint32_t QK_SW = D == 32 ? kSw64 : kSw32;
   static constexpr uint32_t QK_SBO = 8 * D * 2;  // 8 rows x row bytes
   static constexpr int S_COL = 0;               // S of tile t at t*64
   static constexpr int P_COL = 192;             // P of tile t at 192 + t*32
   static constexpr int O_COL = 288;             // O of tile t at 288 + t*NPV
   static_assert(NT <= 3 && O_COL + NT * NPV <= 512, "TMEM budget");
-  static_assert(NS >= 2, "pipeline depth");
-  static_assert(STAGE % 1024 == 0 && (K_BYTES + V_BYTES) % 1024 == 0, "alignment");
+  static_assert(NA >= 2, "pipeline depth");
+  static_assert(A_BYTES % 1024 == 0 && V_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "alignment");
 };
 
 struct AttnArgs {
@@ -87,10 +112,14 @@ template <int D, int TR, int TQ, bool BF32>
 struct AttnSmem {
   using Cfg = AttnCfg<D, TR, TQ, BF32>;
   alignas(1024) uint8_t q[Cfg::NT][Cfg::Q_BYTES];
-  alignas(1024) uint8_t stage[Cfg::NS][Cfg::STAGE];
+  alignas(1024) uint8_t ident[BF32 ? 1024 : Cfg::BK * 128];  // f16 identity (BK x BK, K-major SW128)
+  alignas(1024) uint8_t ring_a[Cfg::NA][Cfg::A_BYTES];
+  alignas(1024) uint8_t ring_b[Cfg::NB][Cfg::VB_BYTES];
   uint64_t bar_q;
-  uint64_t kv_full[Cfg::NS];
-  uint64_t kv_empty[Cfg::NS];  // one commit per tile issuer
+  uint64_t a_full[Cfg::NA];
+  uint64_t a_empty[Cfg::NA];   // one commit per tile issuer (after QK^T and the softmax's bias read)
+  uint64_t b_full[Cfg::NB];
+  uint64_t b_empty[Cfg::NB];   // one commit per tile issuer (after PV)
   uint64_t s_full[Cfg::NT];    // QK^T of the block landed in S
   uint64_t s_free[Cfg::NT];    // the softmax has loaded S (it may be overwritten)
   uint64_t p_full[Cfg::NT];    // P of the block written
@@ -98,6 +127,9 @@ struct AttnSmem {
   uint64_t o_full[Cfg::NT];    // the last PV finished
   uint32_t tmem_base;
   int abort;
+#ifdef TOPS_TRACE
+  long long t_qk[Cfg::NT];
+#endif
 };
 
 template <typename T, int D, int TR, int TQ, bool BF32>
@@ -107,7 +139,7 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
                 const __grid_constant__ CUtensorMap map_b, AttnArgs a) {
   using Cfg = AttnCfg<D, TR, TQ, BF32>;
   using E = Elem<T>;
-  constexpr int NS = Cfg::NS, NT = Cfg::NT, BK = Cfg::BK;
+  constexpr int NA = Cfg::NA, NB = Cfg::NB, NT = Cfg::NT, BK = Cfg::BK;
   extern __shared__ uint8_t smem_raw[];
   auto& sm = *reinterpret_cast<AttnSmem<D, TR, TQ, BF32>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                             ~uintptr_t(1023));
@@ -118,19 +150,32 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
   const int nkb = (a.Nk + BK - 1) / BK;
   const int H = a.H;
   TOPS_TDECL();
-  auto kv_tile = [&](int s, int r) { return sm.stage[s] + TQ * Cfg::B_BYTES + r * (Cfg::K_BYTES + Cfg::V_BYTES); };
+  auto k_tile = [&](int s, int r) { return sm.ring_a[s] + TQ * Cfg::B_BYTES + r * Cfg::K_BYTES; };
+  auto v_tile = [&](int s, int r) { return sm.ring_b[s] + r * Cfg::V_BYTES; };
+  constexpr int PAD_ROWS = Cfg::NPV - D - 1;
 
   // zero the padding rows (D+1 .. NPV-1) of every V^T operand tile once (32 words per 128 B row)
-  for (int idx = threadIdx.x; idx < NS * TR * 15 * 32; idx += blockDim.x) {
-    const int w = idx & 31, rowp = (idx >> 5) % 15, rs = idx / (15 * 32);
-    uint32_t* v = reinterpret_cast<uint32_t*>(kv_tile(rs / TR, rs % TR) + Cfg::K_BYTES);
+  for (int idx = threadIdx.x; idx < NB * TR * PAD_ROWS * 32; idx += blockDim.x) {
+    const int w = idx & 31, rowp = (idx >> 5) % PAD_ROWS, rs = idx / (PAD_ROWS * 32);
+    uint32_t* v = reinterpret_cast<uint32_t*>(v_tile(rs / TR, rs % TR));
     v[(D + 1 + rowp) * 32 + w] = 0u;
+  }
+  if (!BF32) {
+    // identity: element (n, k) of the BK x BK K-major SW128 tile at n*128 + ((k/8 ^ n%8) * 16) + (k%8)*2
+    for (int w = threadIdx.x; w < BK * 32; w += blockDim.x) {
+      const int n = w >> 5, c = (w & 31) >> 2, k0 = ((c ^ (n & 7)) << 3) + ((w & 3) << 1);
+      reinterpret_cast<uint32_t*>(sm.ident)[w] = (k0 == n ? 0x3C00u : 0u) | (k0 + 1 == n ? 0x3C000000u : 0u);
+    }
   }
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_q, 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], NT);
+    for (int s = 0; s < NA; ++s) {
+      mbar_init(&sm.a_full[s], 1);
+      mbar_init(&sm.a_empty[s], NT);
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&sm.b_full[s], 1);
+      mbar_init(&sm.b_empty[s], NT);
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&sm.s_full[t], 1);
@@ -161,25 +206,33 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
       mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
       for (int t = 0; t < NT; ++t)
         tma_load_3d(sm.q[t], &map_q, &sm.bar_q, 0, q0 + (t % TQ) * 128, (row0 + t / TQ) * H + h);
-      for (int j = 0; j < nkb; ++j) {
-        const int s = j % NS;
-        TOPS_TCLK(te0);
-        if (!mbar_wait(&sm.kv_empty[s], ((j / NS) & 1) ^ 1, abort, 201)) break;
-        TOPS_TCLK(te1);
-        TOPS_TADD(7, te0, te1);
-        mbar_expect_tx(&sm.kv_full[s], Cfg::STAGE_TX);
-        const int k0 = j * BK;
-        for (int qb = 0; qb < TQ; ++qb) {
-          uint8_t* bt = sm.stage[s] + qb * Cfg::B_BYTES;
-          tma_load_3d(bt, &map_b, &sm.kv_full[s], k0, q0 + qb * 128, h);
-          if (BF32) tma_load_3d(bt + 16384, &map_b, &sm.kv_full[s], k0 + 32, q0 + qb * 128, h);
+      // ring A of block j, then ring B of block j-1 (V is consumed a block after K)
+      for (int j = 0; j <= nkb; ++j) {
+        if (j < nkb) {
+          const int s = j % NA;
+          TOPS_TCLK(te0);
+          if (!mbar_wait(&sm.a_empty[s], ((j / NA) & 1) ^ 1, abort, 201)) break;
+          TOPS_TCLK(te1);
+          TOPS_TADD(7, te0, te1);
+          mbar_expect_tx(&sm.a_full[s], Cfg::A_BYTES);
+          const int k0 = j * BK;
+          for (int qb = 0; qb < TQ; ++qb) {
+            uint8_t* bt = sm.ring_a[s] + qb * Cfg::B_BYTES;
+            tma_load_3d(bt, &map_b, &sm.a_full[s], k0, q0 + qb * 128, h);
+            if (BF32) tma_load_3d(bt + 16384, &map_b, &sm.a_full[s], k0 + 32, q0 + qb * 128, h);
+          }
+          for (int r = 0; r < TR; ++r) tma_load_3d(k_tile(s, r), &map_k, &sm.a_full[s], 0, k0, (row0 + r) * H + h);
         }
-        for (int r = 0; r < TR; ++r) {
-          uint8_t* kt = kv_tile(s, r);
-          const int rh = (row0 + r) * H + h;
-          tma_load_3d(kt, &map_k, &sm.kv_full[s], 0, k0, rh);
-          tma_load_3d(kt + Cfg::K_BYTES, &map_v, &sm.kv_full[s], k0, 0, rh);
-          tma_load_2d(kt + Cfg::K_BYTES + D * 128, &map_m, &sm.kv_full[s], k0, row0 + r);
+        if (j >= 1) {
+          const int jb = j - 1, s = jb % NB;
+          if (!mbar_wait(&sm.b_empty[s], ((jb / NB) & 1) ^ 1, abort, 211)) break;
+          mbar_expect_tx(&sm.b_full[s], Cfg::VB_TX);
+          const int k0 = jb * BK;
+          for (int r = 0; r < TR; ++r) {
+            uint8_t* vt = v_tile(s, r);
+            tma_load_3d(vt, &map_v, &sm.b_full[s], k0, 0, (row0 + r) * H + h);
+            tma_load_2d(vt + D * 128, &map_m, &sm.b_full[s], k0, row0 + r);
+          }
         }
       }
     }
@@ -194,42 +247,63 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       const uint32_t p_tmem = tbase + Cfg::P_COL + t * 32;
       const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
-      auto issue_pv = [&](int jp) {
-        const uint32_t vb = smem_u32(kv_tile(jp % NS, t / TQ) + Cfg::K_BYTES);
+      auto issue_pv = [&](int jp) -> bool {
+        if (!mbar_wait(&sm.b_full[jp % NB], (jp / NB) & 1, abort, 212)) return false;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(v_tile(jp % NB, t / TQ));
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
           mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, jp > 0 || kk > 0);
         mma_commit(&sm.pv_done[t]);
         if (jp == nkb - 1) mma_commit(&sm.o_full[t]);
-        mma_commit(&sm.kv_empty[jp % NS]);
+        mma_commit(&sm.b_empty[jp % NB]);
+        return true;
       };
       bool ok = mbar_wait(&sm.bar_q, 0, abort, 202);
       for (int j = 0; ok && j < nkb; ++j) {
-        const int s = j % NS;
+        const int s = j % NA;
         TOPS_TCLK(tk0);
-        if (!mbar_wait(&sm.kv_full[s], (j / NS) & 1, abort, 203)) break;
-        if (j > 0 && !mbar_wait(&sm.s_free[t], (j - 1) & 1, abort, 204)) break;
+        if (j > 0) {
+          if (!mbar_wait(&sm.s_free[t], (j - 1) & 1, abort, 204)) break;
+          // fp32 bias (read by the softmax): this tile is done with ring-A slot j-1 once
+          // its QK^T (the commit waits for it) and its softmax's bias read (s_free) are done
+          if (BF32) mma_commit(&sm.a_empty[(j - 1) % NA]);
+        }
+        if (!mbar_wait(&sm.a_full[s], (j / NA) & 1, abort, 203)) break;
         TOPS_TCLK(tk1);
         TOPS_TADD(4, tk0, tk1);
         tc_fence_after();
-        const uint32_t ka = smem_u32(kv_tile(s, t / TQ));
+        const uint32_t ka = smem_u32(k_tile(s, t / TQ));
+        if (!BF32) {
+          // f16 bias: the tensor core adds it, S = bias x I + Q K^T (exact: I is the
+          // identity, products and sums in fp32), so the softmax reads S ready-biased
+          const uint32_t ba = smem_u32(sm.ring_a[s] + (t % TQ) * Cfg::B_BYTES), ia = smem_u32(sm.ident);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_ss(s_tmem, make_smem_desc(ba + kk * 32, 16, 1024, kSw128), make_smem_desc(ia + kk * 32, 16, 1024, kSw128),
+                   idesc_qk, kk > 0);
+        }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
-                 make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_qk, kk > 0);
+                 make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_qk, !BF32 || kk > 0);
         mma_commit(&sm.s_full[t]);
+        if (!BF32) mma_commit(&sm.a_empty[s]);  // K and the bias tile consumed once these MMAs finish
+#ifdef TOPS_TRACE
+        { TOPS_TCLK(tq); *reinterpret_cast<volatile long long*>(&sm.t_qk[t]) = tq; }
+#endif
         if (j > 0) {
           TOPS_TCLK(tp0);
           if (!mbar_wait(&sm.p_full[t], (j - 1) & 1, abort, 205)) break;
           TOPS_TCLK(tp1);
           TOPS_TADD(5, tp0, tp1);
           tc_fence_after();
-          issue_pv(j - 1);
+          if (!issue_pv(j - 1)) break;
         }
         if (j == nkb - 1) {
           if (!mbar_wait(&sm.p_full[t], j & 1, abort, 205)) break;
           tc_fence_after();
-          issue_pv(j);
+          if (!issue_pv(j)) break;
         }
       }
     }
@@ -244,20 +318,24 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
     float m_use = 0.f;
     bool ok = true;
     for (int j = 0; ok && j < nkb; ++j) {
-      const int s = j % NS;
+      const int s = j % NA;
       TOPS_TCLK(ts0);
       if (!mbar_wait(&sm.s_full[t], j & 1, abort, 206)) { ok = false; break; }
-      if (!mbar_wait(&sm.kv_full[s], (j / NS) & 1, abort, 210)) { ok = false; break; }  // bias tile visible
+      if (BF32 && !mbar_wait(&sm.a_full[s], (j / NA) & 1, abort, 210)) { ok = false; break; }  // bias visible
       TOPS_TCLK(ts1);
+#ifdef TOPS_TRACE
+      if (lane == 0 && wq == 0) TOPS_TADD(6, *reinterpret_cast<volatile long long*>(&sm.t_qk[t]), ts1);
+#endif
       tc_fence_after();
-      const uint8_t* brow = sm.stage[s] + qb * Cfg::B_BYTES;
-      // x = S + bias (log2 units), packed to f16 pairs. S is read in two 32-column halves.
+      // x = S + bias (log2 units) packed to f16 pairs. f16 bias: already in S (added by
+      // the tensor core); fp32 bias: added here from the ring-A tile.
       __half2 xh[32];
+      if (BF32) {
+        const uint8_t* brow = sm.ring_a[s] + qb * Cfg::B_BYTES;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[32];
-        tmem_ld32(lane_addr + Cfg::S_COL + t * 64 + half * 32, sv);
-        if (BF32) {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[32];
+          tmem_ld32(lane_addr + Cfg::S_COL + t * 64 + half * 32, sv);
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
             const float4 bf = *reinterpret_cast<const float4*>(brow + half * 16384 + sw128_off(qrow, ch));
@@ -266,20 +344,12 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
             xh[half * 16 + ch * 2 + 1] =
                 __floats2half2_rn(__uint_as_float(sv[ch * 4 + 2]) + bf.z, __uint_as_float(sv[ch * 4 + 3]) + bf.w);
           }
-        } else {
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int ch = half * 4 + cc;
-            const uint4 bu = *reinterpret_cast<const uint4*>(brow + sw128_off(qrow, ch));
-            const uint32_t b4[4] = {bu.x, bu.y, bu.z, bu.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = cc * 8 + 2 * e;
-              xh[half * 16 + cc * 4 + e] = __hadd2(__floats2half2_rn(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])),
-                                                   *reinterpret_cast<const __half2*>(&b4[e]));
-            }
-          }
         }
+      } else {
+        uint32_t sv[64];
+        tmem_ld64(lane_addr + Cfg::S_COL + t * 64, sv);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) xh[c] = __floats2half2_rn(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
       }
       // S consumed: QK^T of the next block may overwrite it
       tc_fence_before();
@@ -326,11 +396,14 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
         }
       }
       const __half2 mh = __float2half2_rn(m_use);  // exact: m_use is an f16 value
+      // 2/5 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
+      // the XU pipe (2 issues per f16 pair) and the FMA pipe then finish together.
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const __half2 d = __hsub2(xh[c], mh);
-        pk[c] = ex2_f16x2(*reinterpret_cast<const uint32_t*>(&d));
+        const uint32_t du = *reinterpret_cast<const uint32_t*>(&d);
+        pk[c] = (kPolyExp && TOPS_POLY_PICK(c)) ? ex2_poly_f16x2(du) : ex2_f16x2(du);
       }
       TOPS_TCLK(ts3);
       if (j > 0 && !waited) {
