@@ -116,6 +116,7 @@ struct AttnSmem {
   alignas(1024) uint8_t ring_a[Cfg::NA][Cfg::A_BYTES];
   alignas(1024) uint8_t ring_b[Cfg::NB][Cfg::VB_BYTES];
   uint64_t bar_q;
+  uint64_t q_empty;            // one commit per tile issuer (after the unit's last QK^T)
   uint64_t a_full[Cfg::NA];
   uint64_t a_empty[Cfg::NA];   // one commit per tile issuer (after QK^T and the softmax's bias read)
   uint64_t b_full[Cfg::NB];
@@ -124,7 +125,8 @@ struct AttnSmem {
   uint64_t s_free[Cfg::NT];    // the softmax has loaded S (it may be overwritten)
   uint64_t p_full[Cfg::NT];    // P of the block written
   uint64_t pv_done[Cfg::NT];   // PV of the block finished (P reusable, O stable)
-  uint64_t o_full[Cfg::NT];    // the last PV finished
+  uint64_t o_full[Cfg::NT];    // the last PV of the unit finished
+  uint64_t o_empty[Cfg::NT];   // the epilogue has read O (the next unit may overwrite it)
   uint32_t tmem_base;
   int abort;
 #ifdef TOPS_TRACE
@@ -144,9 +146,6 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
   auto& sm = *reinterpret_cast<AttnSmem<D, TR, TQ, BF32>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                             ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.z;
-  const int row0 = blockIdx.y * TR;
-  const int q0 = blockIdx.x * (128 * TQ);
   const int nkb = (a.Nk + BK - 1) / BK;
   const int H = a.H;
   TOPS_TDECL();
@@ -169,6 +168,7 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
   }
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_q, 1);
+    mbar_init(&sm.q_empty, NT);
     for (int s = 0; s < NA; ++s) {
       mbar_init(&sm.a_full[s], 1);
       mbar_init(&sm.a_empty[s], NT);
@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
       mbar_init(&sm.p_full[t], 4);
       mbar_init(&sm.pv_done[t], 1);
       mbar_init(&sm.o_full[t], 1);
+      mbar_init(&sm.o_empty[t], 4);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -195,6 +196,21 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
   const uint32_t tbase = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
+  // Persistent: CTA b takes work units b, b + gridDim.x, ... A unit is TR rows x TQ
+  // 128-query blocks of one head (x fastest: the CTAs running together share the bias
+  // tiles of a head and the K/V of a row in L2). Ring slots and barrier phases run on
+  // across units (g = blocks processed by this CTA so far, lu = units so far), so the
+  // producer streams the next unit's tiles while the current one finishes.
+  const int n_qb = (a.Nq + 128 * TQ - 1) / (128 * TQ);
+  const int n_rg = (a.R + TR - 1) / TR;
+  const int n_units = n_qb * n_rg * a.H;
+  auto coords = [&](int u, int& q0, int& row0, int& h) {
+    q0 = (u % n_qb) * (128 * TQ);
+    const int rest = u / n_qb;
+    row0 = (rest % n_rg) * TR;
+    h = rest / n_rg;
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
@@ -203,35 +219,45 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
       tma_prefetch_desc(&map_v);
       tma_prefetch_desc(&map_m);
       tma_prefetch_desc(&map_b);
-      mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
-      for (int t = 0; t < NT; ++t)
-        tma_load_3d(sm.q[t], &map_q, &sm.bar_q, 0, q0 + (t % TQ) * 128, (row0 + t / TQ) * H + h);
-      // ring A of block j, then ring B of block j-1 (V is consumed a block after K)
-      for (int j = 0; j <= nkb; ++j) {
-        if (j < nkb) {
-          const int s = j % NA;
-          TOPS_TCLK(te0);
-          if (!mbar_wait(&sm.a_empty[s], ((j / NA) & 1) ^ 1, abort, 201)) break;
-          TOPS_TCLK(te1);
-          TOPS_TADD(7, te0, te1);
-          mbar_expect_tx(&sm.a_full[s], Cfg::A_BYTES);
-          const int k0 = j * BK;
-          for (int qb = 0; qb < TQ; ++qb) {
-            uint8_t* bt = sm.ring_a[s] + qb * Cfg::B_BYTES;
-            tma_load_3d(bt, &map_b, &sm.a_full[s], k0, q0 + qb * 128, h);
-            if (BF32) tma_load_3d(bt + 16384, &map_b, &sm.a_full[s], k0 + 32, q0 + qb * 128, h);
+      bool ok = true;
+      int g = 0, lu = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+        int q0, row0, h;
+        coords(u, q0, row0, h);
+        // ring A of block j, then ring B of block j-1 (V is consumed a block after K); the
+        // unit's Q tiles after its first ring-A block, once the previous unit's QK^T is done
+        for (int j = 0; j <= nkb; ++j) {
+          if (j < nkb) {
+            const int gg = g + j, s = gg % NA;
+            TOPS_TCLK(te0);
+            if (!mbar_wait(&sm.a_empty[s], ((gg / NA) & 1) ^ 1, abort, 201)) { ok = false; break; }
+            TOPS_TCLK(te1);
+            TOPS_TADD(7, te0, te1);
+            mbar_expect_tx(&sm.a_full[s], Cfg::A_BYTES);
+            const int k0 = j * BK;
+            for (int qb = 0; qb < TQ; ++qb) {
+              uint8_t* bt = sm.ring_a[s] + qb * Cfg::B_BYTES;
+              tma_load_3d(bt, &map_b, &sm.a_full[s], k0, q0 + qb * 128, h);
+              if (BF32) tma_load_3d(bt + 16384, &map_b, &sm.a_full[s], k0 + 32, q0 + qb * 128, h);
+            }
+            for (int r = 0; r < TR; ++r) tma_load_3d(k_tile(s, r), &map_k, &sm.a_full[s], 0, k0, (row0 + r) * H + h);
           }
-          for (int r = 0; r < TR; ++r) tma_load_3d(k_tile(s, r), &map_k, &sm.a_full[s], 0, k0, (row0 + r) * H + h);
-        }
-        if (j >= 1) {
-          const int jb = j - 1, s = jb % NB;
-          if (!mbar_wait(&sm.b_empty[s], ((jb / NB) & 1) ^ 1, abort, 211)) break;
-          mbar_expect_tx(&sm.b_full[s], Cfg::VB_TX);
-          const int k0 = jb * BK;
-          for (int r = 0; r < TR; ++r) {
-            uint8_t* vt = v_tile(s, r);
-            tma_load_3d(vt, &map_v, &sm.b_full[s], k0, 0, (row0 + r) * H + h);
-            tma_load_2d(vt + D * 128, &map_m, &sm.b_full[s], k0, row0 + r);
+          if (j == 0) {
+            if (!mbar_wait(&sm.q_empty, (lu & 1) ^ 1, abort, 213)) { ok = false; break; }
+            mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
+            for (int t = 0; t < NT; ++t)
+              tma_load_3d(sm.q[t], &map_q, &sm.bar_q, 0, q0 + (t % TQ) * 128, (row0 + t / TQ) * H + h);
+          }
+          if (j >= 1) {
+            const int gb = g + j - 1, s = gb % NB;
+            if (!mbar_wait(&sm.b_empty[s], ((gb / NB) & 1) ^ 1, abort, 211)) { ok = false; break; }
+            mbar_expect_tx(&sm.b_full[s], Cfg::VB_TX);
+            const int k0 = (j - 1) * BK;
+            for (int r = 0; r < TR; ++r) {
+              uint8_t* vt = v_tile(s, r);
+              tma_load_3d(vt, &map_v, &sm.b_full[s], k0, 0, (row0 + r) * H + h);
+              tma_load_2d(vt + D * 128, &map_m, &sm.b_full[s], k0, row0 + r);
+            }
           }
         }
       }
@@ -247,63 +273,72 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       const uint32_t p_tmem = tbase + Cfg::P_COL + t * 32;
       const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
-      auto issue_pv = [&](int jp) -> bool {
-        if (!mbar_wait(&sm.b_full[jp % NB], (jp / NB) & 1, abort, 212)) return false;
+      int lu = 0;
+      // PV of block jl of the unit (gb = its ring counter)
+      auto issue_pv = [&](int gb, int jl) -> bool {
+        if (!mbar_wait(&sm.b_full[gb % NB], (gb / NB) & 1, abort, 212)) return false;
+        // the first PV of a unit overwrites O: the previous unit's epilogue must have read it
+        if (jl == 0 && lu > 0 && !mbar_wait(&sm.o_empty[t], (lu - 1) & 1, abort, 214)) return false;
         tc_fence_after();
-        const uint32_t vb = smem_u32(v_tile(jp % NB, t / TQ));
+        const uint32_t vb = smem_u32(v_tile(gb % NB, t / TQ));
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, jp > 0 || kk > 0);
+          mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, jl > 0 || kk > 0);
         mma_commit(&sm.pv_done[t]);
-        if (jp == nkb - 1) mma_commit(&sm.o_full[t]);
-        mma_commit(&sm.b_empty[jp % NB]);
+        if (jl == nkb - 1) mma_commit(&sm.o_full[t]);
+        mma_commit(&sm.b_empty[gb % NB]);
         return true;
       };
-      bool ok = mbar_wait(&sm.bar_q, 0, abort, 202);
-      for (int j = 0; ok && j < nkb; ++j) {
-        const int s = j % NA;
-        TOPS_TCLK(tk0);
-        if (j > 0) {
-          if (!mbar_wait(&sm.s_free[t], (j - 1) & 1, abort, 204)) break;
-          // fp32 bias (read by the softmax): this tile is done with ring-A slot j-1 once
-          // its QK^T (the commit waits for it) and its softmax's bias read (s_free) are done
-          if (BF32) mma_commit(&sm.a_empty[(j - 1) % NA]);
-        }
-        if (!mbar_wait(&sm.a_full[s], (j / NA) & 1, abort, 203)) break;
-        TOPS_TCLK(tk1);
-        TOPS_TADD(4, tk0, tk1);
-        tc_fence_after();
-        const uint32_t ka = smem_u32(k_tile(s, t / TQ));
-        if (!BF32) {
-          // f16 bias: the tensor core adds it, S = bias x I + Q K^T (exact: I is the
-          // identity, products and sums in fp32), so the softmax reads S ready-biased
-          const uint32_t ba = smem_u32(sm.ring_a[s] + (t % TQ) * Cfg::B_BYTES), ia = smem_u32(sm.ident);
+      bool ok = true;
+      int g = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+        if (!mbar_wait(&sm.bar_q, lu & 1, abort, 202)) break;
+        for (int j = 0; j < nkb; ++j) {
+          const int gg = g + j, s = gg % NA;
+          TOPS_TCLK(tk0);
+          if (gg > 0) {
+            if (!mbar_wait(&sm.s_free[t], (gg - 1) & 1, abort, 204)) { ok = false; break; }
+            // fp32 bias (read by the softmax): this tile is done with ring-A slot gg-1 once
+            // its QK^T (the commit waits for it) and its softmax's bias read (s_free) are done
+            if (BF32) mma_commit(&sm.a_empty[(gg - 1) % NA]);
+          }
+          if (!mbar_wait(&sm.a_full[s], (gg / NA) & 1, abort, 203)) { ok = false; break; }
+          TOPS_TCLK(tk1);
+          TOPS_TADD(4, tk0, tk1);
+          tc_fence_after();
+          const uint32_t ka = smem_u32(k_tile(s, t / TQ));
+          if (!BF32) {
+            // f16 bias: the tensor core adds it, S = bias x I + Q K^T (exact: I is the
+            // identity, products and sums in fp32), so the softmax reads S ready-biased
+            const uint32_t ba = smem_u32(sm.ring_a[s] + (t % TQ) * Cfg::B_BYTES), ia = smem_u32(sm.ident);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            mma_ss(s_tmem, make_smem_desc(ba + kk * 32, 16, 1024, kSw128), make_smem_desc(ia + kk * 32, 16, 1024, kSw128),
-                   idesc_qk, kk > 0);
-        }
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_ss(s_tmem, make_smem_desc(ba + kk * 32, 16, 1024, kSw128),
+                     make_smem_desc(ia + kk * 32, 16, 1024, kSw128), idesc_qk, kk > 0);
+          }
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
-                 make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_qk, !BF32 || kk > 0);
-        mma_commit(&sm.s_full[t]);
-        if (!BF32) mma_commit(&sm.a_empty[s]);  // K and the bias tile consumed once these MMAs finish
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
+                   make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_qk, !BF32 || kk > 0);
+          mma_commit(&sm.s_full[t]);
+          if (!BF32) mma_commit(&sm.a_empty[s]);  // K and the bias tile consumed once these MMAs finish
+          if (j == nkb - 1) mma_commit(&sm.q_empty);  // Q of this unit no longer needed
 #ifdef TOPS_TRACE
-        { TOPS_TCLK(tq); *reinterpret_cast<volatile long long*>(&sm.t_qk[t]) = tq; }
+          { TOPS_TCLK(tq); *reinterpret_cast<volatile long long*>(&sm.t_qk[t]) = tq; }
 #endif
-        if (j > 0) {
-          TOPS_TCLK(tp0);
-          if (!mbar_wait(&sm.p_full[t], (j - 1) & 1, abort, 205)) break;
-          TOPS_TCLK(tp1);
-          TOPS_TADD(5, tp0, tp1);
-          tc_fence_after();
-          if (!issue_pv(j - 1)) break;
-        }
-        if (j == nkb - 1) {
-          if (!mbar_wait(&sm.p_full[t], j & 1, abort, 205)) break;
-          tc_fence_after();
-          if (!issue_pv(j)) break;
+          if (j > 0) {
+            TOPS_TCLK(tp0);
+            if (!mbar_wait(&sm.p_full[t], (gg - 1) & 1, abort, 205)) { ok = false; break; }
+            TOPS_TCLK(tp1);
+            TOPS_TADD(5, tp0, tp1);
+            tc_fence_after();
+            if (!issue_pv(gg - 1, j - 1)) { ok = false; break; }
+          }
+          if (j == nkb - 1) {
+            if (!mbar_wait(&sm.p_full[t], gg & 1, abort, 205)) { ok = false; break; }
+            tc_fence_after();
+            if (!issue_pv(gg, j)) { ok = false; break; }
+          }
         }
       }
     }
@@ -315,136 +350,146 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
     const int qb = t % TQ;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     const uint32_t oaddr = lane_addr + Cfg::O_COL + t * Cfg::NPV;
-    float m_use = 0.f;
     bool ok = true;
-    for (int j = 0; ok && j < nkb; ++j) {
-      const int s = j % NA;
-      TOPS_TCLK(ts0);
-      if (!mbar_wait(&sm.s_full[t], j & 1, abort, 206)) { ok = false; break; }
-      if (BF32 && !mbar_wait(&sm.a_full[s], (j / NA) & 1, abort, 210)) { ok = false; break; }  // bias visible
-      TOPS_TCLK(ts1);
+    int g = 0, lu = 0;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+      int q0, row0, h;
+      coords(u, q0, row0, h);
+      float m_use = 0.f;
+      for (int j = 0; j < nkb; ++j) {
+        const int gg = g + j, s = gg % NA;
+        TOPS_TCLK(ts0);
+        if (!mbar_wait(&sm.s_full[t], gg & 1, abort, 206)) { ok = false; break; }
+        if (BF32 && !mbar_wait(&sm.a_full[s], (gg / NA) & 1, abort, 210)) { ok = false; break; }  // bias visible
+        TOPS_TCLK(ts1);
 #ifdef TOPS_TRACE
-      if (lane == 0 && wq == 0) TOPS_TADD(6, *reinterpret_cast<volatile long long*>(&sm.t_qk[t]), ts1);
+        if (lane == 0 && wq == 0) TOPS_TADD(6, *reinterpret_cast<volatile long long*>(&sm.t_qk[t]), ts1);
 #endif
-      tc_fence_after();
-      // x = S + bias (log2 units) packed to f16 pairs. f16 bias: already in S (added by
-      // the tensor core); fp32 bias: added here from the ring-A tile.
-      __half2 xh[32];
-      if (BF32) {
-        const uint8_t* brow = sm.ring_a[s] + qb * Cfg::B_BYTES;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[32];
-          tmem_ld32(lane_addr + Cfg::S_COL + t * 64 + half * 32, sv);
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const float4 bf = *reinterpret_cast<const float4*>(brow + half * 16384 + sw128_off(qrow, ch));
-            xh[half * 16 + ch * 2] =
-                __floats2half2_rn(__uint_as_float(sv[ch * 4]) + bf.x, __uint_as_float(sv[ch * 4 + 1]) + bf.y);
-            xh[half * 16 + ch * 2 + 1] =
-                __floats2half2_rn(__uint_as_float(sv[ch * 4 + 2]) + bf.z, __uint_as_float(sv[ch * 4 + 3]) + bf.w);
-          }
-        }
-      } else {
-        uint32_t sv[64];
-        tmem_ld64(lane_addr + Cfg::S_COL + t * 64, sv);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) xh[c] = __floats2half2_rn(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
-      }
-      // S consumed: QK^T of the next block may overwrite it
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_free[t]);
-      TOPS_TCLK(ts2);
-      __half2 mt[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) mt[c] = __hmax2(xh[2 * c], xh[2 * c + 1]);
-#pragma unroll
-      for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-        for (int c = 0; c < w; ++c) mt[c] = __hmax2(mt[c], mt[c + w]);
-      const float mx = fmaxf(__low2float(mt[0]), __high2float(mt[0]));
-      // P(j) overwrites P(j-1), and an O rescale needs O stable: both need PV(j-1) done.
-      // The softmax of block j-1 already waited for PV(j-2), so pv_done is at most one
-      // phase behind and the parity wait is exact.
-      bool waited = false;
-      if (j == 0) {
-        m_use = mx;
-      } else {
-        const bool need = mx > m_use + 8.0f;
-        if (__any_sync(0xffffffffu, need)) {
-          if (!mbar_wait(&sm.pv_done[t], (j - 1) & 1, abort, 208)) { ok = false; break; }
-          waited = true;
-          tc_fence_after();
-          const float alpha = need ? ex2_approx(m_use - mx) : 1.0f;
-          if (need) m_use = mx;
-          uint32_t o[Cfg::NPV];
-          if (D == 32) {
-            tmem_ld32(oaddr, o);
-            tmem_ld16(oaddr + 32, o + 32);
-          } else {
-            tmem_ld32(oaddr, o);
-          }
-#pragma unroll
-          for (int c = 0; c < Cfg::NPV; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          if (D == 32) {
-            tmem_st32(oaddr, o);
-            tmem_st16(oaddr + 32, o + 32);
-          } else {
-            tmem_st32(oaddr, o);
-          }
-        }
-      }
-      const __half2 mh = __float2half2_rn(m_use);  // exact: m_use is an f16 value
-      // 2/5 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
-      // the XU pipe (2 issues per f16 pair) and the FMA pipe then finish together.
-      uint32_t pk[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const __half2 d = __hsub2(xh[c], mh);
-        const uint32_t du = *reinterpret_cast<const uint32_t*>(&d);
-        pk[c] = (kPolyExp && TOPS_POLY_PICK(c)) ? ex2_poly_f16x2(du) : ex2_f16x2(du);
-      }
-      TOPS_TCLK(ts3);
-      if (j > 0 && !waited) {
-        if (!mbar_wait(&sm.pv_done[t], (j - 1) & 1, abort, 209)) { ok = false; break; }
         tc_fence_after();
+        // x = S + bias (log2 units) packed to f16 pairs. f16 bias: already in S (added by
+        // the tensor core); fp32 bias: added here from the ring-A tile.
+        __half2 xh[32];
+        if (BF32) {
+          const uint8_t* brow = sm.ring_a[s] + qb * Cfg::B_BYTES;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t sv[32];
+            tmem_ld32(lane_addr + Cfg::S_COL + t * 64 + half * 32, sv);
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const float4 bf = *reinterpret_cast<const float4*>(brow + half * 16384 + sw128_off(qrow, ch));
+              xh[half * 16 + ch * 2] =
+                  __floats2half2_rn(__uint_as_float(sv[ch * 4]) + bf.x, __uint_as_float(sv[ch * 4 + 1]) + bf.y);
+              xh[half * 16 + ch * 2 + 1] =
+                  __floats2half2_rn(__uint_as_float(sv[ch * 4 + 2]) + bf.z, __uint_as_float(sv[ch * 4 + 3]) + bf.w);
+            }
+          }
+        } else {
+          uint32_t sv[64];
+          tmem_ld64(lane_addr + Cfg::S_COL + t * 64, sv);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) xh[c] = __floats2half2_rn(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
+        }
+        // S consumed: QK^T of the next block may overwrite it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[t]);
+        TOPS_TCLK(ts2);
+        __half2 mt[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) mt[c] = __hmax2(xh[2 * c], xh[2 * c + 1]);
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int c = 0; c < w; ++c) mt[c] = __hmax2(mt[c], mt[c + w]);
+        const float mx = fmaxf(__low2float(mt[0]), __high2float(mt[0]));
+        // P(j) overwrites P(j-1), and an O rescale needs O stable: both need PV(j-1) done.
+        // The softmax of block j-1 already waited for PV(j-2), so pv_done is at most one
+        // phase behind and the parity wait is exact.
+        bool waited = false;
+        if (j == 0) {
+          m_use = mx;
+        } else {
+          const bool need = mx > m_use + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            if (!mbar_wait(&sm.pv_done[t], (gg - 1) & 1, abort, 208)) { ok = false; break; }
+            waited = true;
+            tc_fence_after();
+            const float alpha = need ? ex2_approx(m_use - mx) : 1.0f;
+            if (need) m_use = mx;
+            uint32_t o[Cfg::NPV];
+            if (D == 32) {
+              tmem_ld32(oaddr, o);
+              tmem_ld16(oaddr + 32, o + 32);
+            } else {
+              tmem_ld32(oaddr, o);
+            }
+#pragma unroll
+            for (int c = 0; c < Cfg::NPV; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            if (D == 32) {
+              tmem_st32(oaddr, o);
+              tmem_st16(oaddr + 32, o + 32);
+            } else {
+              tmem_st32(oaddr, o);
+            }
+          }
+        }
+        const __half2 mh = __float2half2_rn(m_use);  // exact: m_use is an f16 value
+        // 2/5 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
+        // the XU pipe (2 issues per f16 pair) and the FMA pipe then finish together.
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const __half2 d = __hsub2(xh[c], mh);
+          const uint32_t du = *reinterpret_cast<const uint32_t*>(&d);
+          pk[c] = (kPolyExp && TOPS_POLY_PICK(c)) ? ex2_poly_f16x2(du) : ex2_f16x2(du);
+        }
+        TOPS_TCLK(ts3);
+        if (j > 0 && !waited) {
+          if (!mbar_wait(&sm.pv_done[t], (gg - 1) & 1, abort, 209)) { ok = false; break; }
+          tc_fence_after();
+        }
+        tmem_st32(lane_addr + Cfg::P_COL + t * 32, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[t]);
+        TOPS_TCLK(ts4);
+        if (lane == 0) {
+          TOPS_TADD(0, ts0, ts1);
+          TOPS_TADD(1, ts1, ts2);
+          TOPS_TADD(2, ts2, ts3);
+          TOPS_TADD(3, ts3, ts4);
+        }
       }
-      tmem_st32(lane_addr + Cfg::P_COL + t * 32, pk);
-      tmem_wait_st();
+      // ---------------- epilogue: O / l -> out ----------------
+      const bool got = ok && mbar_wait(&sm.o_full[t], lu & 1, abort, 207);
+      if (!got) ok = false;
+      tc_fence_after();
+      uint32_t o[Cfg::NPV];
+      if (D == 32) {
+        tmem_ld32(oaddr, o);
+        tmem_ld16(oaddr + 32, o + 32);
+      } else {
+        tmem_ld32(oaddr, o);
+      }
+      // O is in registers: the next unit's first PV may overwrite it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full[t]);
-      TOPS_TCLK(ts4);
-      if (lane == 0) {
-        TOPS_TADD(0, ts0, ts1);
-        TOPS_TADD(1, ts1, ts2);
-        TOPS_TADD(2, ts2, ts3);
-        TOPS_TADD(3, ts3, ts4);
+      if (lane == 0) mbar_arrive(&sm.o_empty[t]);
+      const int ri = row0 + t / TQ;
+      const int q = q0 + qb * 128 + qrow;
+      if (got && ri < a.R && q < a.Nq) {
+        const float inv = 1.0f / __uint_as_float(o[D]);
+        uint32_t pk[D / 2];
+#pragma unroll
+        for (int c = 0; c < D / 2; ++c)
+          pk[c] = E::pack2(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+        uint4* dst =
+            reinterpret_cast<uint4*>(static_cast<T*>(a.out) + (static_cast<size_t>(ri) * a.Nq + q) * (H * D) + h * D);
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
-    }
-    // ---------------- epilogue: O / l -> out ----------------
-    const bool got = ok && mbar_wait(&sm.o_full[t], 0, abort, 207);
-    tc_fence_after();
-    uint32_t o[Cfg::NPV];
-    if (D == 32) {
-      tmem_ld32(oaddr, o);
-      tmem_ld16(oaddr + 32, o + 32);
-    } else {
-      tmem_ld32(oaddr, o);
-    }
-    const int ri = row0 + t / TQ;
-    const int q = q0 + qb * 128 + qrow;
-    if (got && ri < a.R && q < a.Nq) {
-      const float inv = 1.0f / __uint_as_float(o[D]);
-      uint32_t pk[D / 2];
-#pragma unroll
-      for (int c = 0; c < D / 2; ++c)
-        pk[c] = E::pack2(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
-      uint4* dst =
-          reinterpret_cast<uint4*>(static_cast<T*>(a.out) + (static_cast<size_t>(ri) * a.Nq + q) * (H * D) + h * D);
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     }
   }
   TOPS_TFLUSH();
