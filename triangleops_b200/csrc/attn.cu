@@ -23,10 +23,12 @@
 // thread busy for ~140 cycles whatever N is (up to N=128), while the tensor core
 // itself can absorb a new small MMA every ~50 cycles when several warps issue. At
 // D=32 the work per key block is many small MMAs (QK^T: D/16, PV: BK/16), so each
-// tile has its OWN issuing warp: the tiles' MMA streams overlap in the tensor core.
+// tile has its OWN issuing threads (one for QK^T, one for PV): the MMA streams overlap
+// in the tensor core.
 //
 // Per CTA: w0 TMA producer (per 64-key block: bias and K tiles into ring A, V^T and
-// mask rows into ring B), w(1+t) MMA issuer of tile t, one softmax warpgroup per tile (one TMEM
+// mask rows into ring B), w(1+t) QK^T and w(1+NT+t) PV issuer of tile t, one softmax
+// warpgroup per tile (one TMEM
 // lane = one query row per thread). TMEM per tile: S (64 fp32 columns), P (32
 // columns of packed f16 pairs, the A operand of PV) and O (D+16 columns). The
 // softmax releases S as soon as it has loaded it, so QK^T(j+1) runs while the
@@ -75,6 +77,10 @@ __device__ unsigned long long g_attn_trace[16];
 template <int D, int TR, int TQ, bool BF32 = false>
 struct AttnCfg {
   static constexpr int NT = TR * TQ;            // tiles (128 queries x 1 row) per CTA
+  // warps: 0 TMA producer, 1..NT QK^T issuers, NT+1..2NT PV issuers, then one softmax
+  // warpgroup per tile (any 4 consecutive warps cover the 4 TMEM lane quarters)
+  static constexpr int SM_WARP0 = 1 + 2 * NT;
+  static constexpr int THREADS = 32 * SM_WARP0 + 128 * NT;
   static constexpr int BK = 64;                 // keys per block
   static constexpr int NPV = D + 16;            // PV N: D value columns + mask row + zero pad
   static constexpr int Q_BYTES = 128 * D * 2;
@@ -135,7 +141,7 @@ struct AttnSmem {
 };
 
 template <typename T, int D, int TR, int TQ, bool BF32>
-__global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
+__global__ void __launch_bounds__(AttnCfg<D, TR, TQ, BF32>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_m,
                 const __grid_constant__ CUtensorMap map_b, AttnArgs a) {
@@ -264,33 +270,13 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
     }
   } else if (warp <= NT) {
     if (lane == 0) {
-      // ---------------- MMA issuer of tile t ----------------
+      // ---------------- QK^T issuer of tile t ----------------
       const int t = warp - 1;
       const uint32_t idesc_qk = make_idesc_f16(128, BK, 0, false, false);  // Q, K are f16
-      // P (ex2 output) and V^T are f16 whatever the IO dtype.
-      const uint32_t idesc_pv = make_idesc_f16(128, Cfg::NPV, 0, false, false);
       const uint32_t qa = smem_u32(sm.q[t]);
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
-      const uint32_t p_tmem = tbase + Cfg::P_COL + t * 32;
-      const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
-      int lu = 0;
-      // PV of block jl of the unit (gb = its ring counter)
-      auto issue_pv = [&](int gb, int jl) -> bool {
-        if (!mbar_wait(&sm.b_full[gb % NB], (gb / NB) & 1, abort, 212)) return false;
-        // the first PV of a unit overwrites O: the previous unit's epilogue must have read it
-        if (jl == 0 && lu > 0 && !mbar_wait(&sm.o_empty[t], (lu - 1) & 1, abort, 214)) return false;
-        tc_fence_after();
-        const uint32_t vb = smem_u32(v_tile(gb % NB, t / TQ));
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, jl > 0 || kk > 0);
-        mma_commit(&sm.pv_done[t]);
-        if (jl == nkb - 1) mma_commit(&sm.o_full[t]);
-        mma_commit(&sm.b_empty[gb % NB]);
-        return true;
-      };
       bool ok = true;
-      int g = 0;
+      int g = 0, lu = 0;
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
         if (!mbar_wait(&sm.bar_q, lu & 1, abort, 202)) break;
         for (int j = 0; j < nkb; ++j) {
@@ -326,25 +312,45 @@ __global__ void __launch_bounds__(128 + 128 * AttnCfg<D, TR, TQ, BF32>::NT, 1)
 #ifdef TOPS_TRACE
           { TOPS_TCLK(tq); *reinterpret_cast<volatile long long*>(&sm.t_qk[t]) = tq; }
 #endif
-          if (j > 0) {
-            TOPS_TCLK(tp0);
-            if (!mbar_wait(&sm.p_full[t], (gg - 1) & 1, abort, 205)) { ok = false; break; }
-            TOPS_TCLK(tp1);
-            TOPS_TADD(5, tp0, tp1);
-            tc_fence_after();
-            if (!issue_pv(gg - 1, j - 1)) { ok = false; break; }
-          }
-          if (j == nkb - 1) {
-            if (!mbar_wait(&sm.p_full[t], gg & 1, abort, 205)) { ok = false; break; }
-            tc_fence_after();
-            if (!issue_pv(gg, j)) { ok = false; break; }
-          }
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp <= 2 * NT) {
+    if (lane == 0) {
+      // ---------------- PV issuer of tile t ----------------
+      // (a thread of its own: one tcgen05.mma occupies the issuing thread ~140 cycles
+      // whatever its N, so QK^T and PV of a tile go out from two threads in parallel)
+      const int t = warp - 1 - NT;
+      // P (ex2 output) and V^T are f16 whatever the IO dtype.
+      const uint32_t idesc_pv = make_idesc_f16(128, Cfg::NPV, 0, false, false);
+      const uint32_t p_tmem = tbase + Cfg::P_COL + t * 32;
+      const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
+      bool ok = true;
+      int g = 0, lu = 0;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+        for (int j = 0; j < nkb; ++j) {
+          const int gg = g + j;
+          TOPS_TCLK(tp0);
+          if (!mbar_wait(&sm.p_full[t], gg & 1, abort, 205)) { ok = false; break; }
+          TOPS_TCLK(tp1);
+          TOPS_TADD(5, tp0, tp1);
+          if (!mbar_wait(&sm.b_full[gg % NB], (gg / NB) & 1, abort, 212)) { ok = false; break; }
+          // the first PV of a unit overwrites O: the previous unit's epilogue must have read it
+          if (j == 0 && lu > 0 && !mbar_wait(&sm.o_empty[t], (lu - 1) & 1, abort, 214)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t vb = smem_u32(v_tile(gg % NB, t / TQ));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, j > 0 || kk > 0);
+          mma_commit(&sm.pv_done[t]);
+          if (j == nkb - 1) mma_commit(&sm.o_full[t]);
+          mma_commit(&sm.b_empty[gg % NB]);
+        }
+      }
+    }
+  } else if (warp >= Cfg::SM_WARP0) {
     // ---------------- softmax warpgroups (one tile each) ----------------
-    const int t = (warp - 4) >> 2;
+    const int t = (warp - Cfg::SM_WARP0) >> 2;
     const int wq = warp & 3;
     const int qrow = wq * 32 + lane;  // TMEM lane == query row within the tile
     const int qb = t % TQ;

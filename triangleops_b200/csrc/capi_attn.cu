@@ -135,7 +135,7 @@ int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q,
   // persistent: one CTA per SM (shared memory and TMEM allow no second), looping over units
   const long long units = static_cast<long long>((Nq + 128 * TQ - 1) / (128 * TQ)) * ((R + TR - 1) / TR) * H;
   const int grid = units < sm_count() ? static_cast<int>(units) : sm_count();
-  kern<<<grid, 128 + 128 * Cfg::NT, smem, st>>>(mq, mk, mv, mm, mb, args);
+  kern<<<grid, Cfg::THREADS, smem, st>>>(mq, mk, mv, mm, mb, args);
   return launch_status();
 }
 
