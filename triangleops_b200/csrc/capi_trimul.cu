@@ -11,13 +11,13 @@ template <typename T, int C>
 int launch_trimul_in(int dtype, const void* x, const void* w, const LnGateArgs& args, cudaStream_t st) {
   CUtensorMap mx, mw;
   if (!map_rows(&mx, dtype, x, args.M, C, 128)) return TOPS_ERR_TMAP;
-  if (!map_rows(&mw, dtype, w, 4 * C, C, 2 * C > 256 ? 256 : 2 * C)) return TOPS_ERR_TMAP;
+  if (!map_rows(&mw, dtype, w, 4 * C, C, C)) return TOPS_ERR_TMAP;  // C-row boxes, placed by half
   const size_t smem = sizeof(TmInSmem<C>) + 1024;
   auto kern = trimul_in_kernel<T, C>;
   set_smem(kern, smem);
   const long long tiles = (args.M + 127) / 128;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 384, smem, st>>>(mx, mw, args);
+  kern<<<grid, 512, smem, st>>>(mx, mw, args);
   return launch_status();
 }
 
@@ -37,7 +37,7 @@ int launch_trimul_out(int dtype, const void* y, const void* x, const void* w, co
   set_smem(kern, smem);
   const long long tiles = (args.M + 127) / 128;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 384, smem, st>>>(my, mx, mw, args);
+  kern<<<grid, 512, smem, st>>>(my, mx, mw, args);
   return launch_status();
 }
 

@@ -26,31 +26,33 @@ struct LnGateArgs {
   const void* residual;  // output phase: nullptr, or [M][C] added to the result (may alias out)
 };
 
-// LayerNorm statistics of a 128 x C row-major (K-major, SW128) staged tile row.
+// LayerNorm statistics of a 128 x C row-major (K-major, SW128) staged tile row
+// (two passes over shared memory, 16-byte chunks: no C-wide register array).
 template <typename T, int C>
 __device__ __forceinline__ void row_stats_kmajor(const uint8_t* tile, int row, float& mean, float& rstd, float eps) {
   using E = Elem<T>;
-  uint32_t pk[C / 2];
-#pragma unroll
-  for (int ka = 0; ka < C / 64; ++ka)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const uint4 u = *reinterpret_cast<const uint4*>(tile + ka * 16384 + sw128_off(row, ch));
-      const int b = ka * 32 + ch * 4;
-      pk[b] = u.x;
-      pk[b + 1] = u.y;
-      pk[b + 2] = u.z;
-      pk[b + 3] = u.w;
-    }
+  auto chunk = [&](int i) {  // chunk i of the row: channels [8i, 8i + 8)
+    return *reinterpret_cast<const uint4*>(tile + (i >> 3) * 16384 + sw128_off(row, i & 7));
+  };
   float s = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < C / 8; ++i) {
+    const uint4 u = chunk(i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int c = 0; c < C / 2; ++c) s += E::lo(pk[c]) + E::hi(pk[c]);
+    for (int e = 0; e < 4; ++e) s += E::lo(w[e]) + E::hi(w[e]);
+  }
   mean = s * (1.0f / C);
   float v = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < C / 8; ++i) {
+    const uint4 u = chunk(i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int c = 0; c < C / 2; ++c) {
-    const float d0 = E::lo(pk[c]) - mean, d1 = E::hi(pk[c]) - mean;
-    v = fmaf(d0, d0, fmaf(d1, d1, v));
+    for (int e = 0; e < 4; ++e) {
+      const float d0 = E::lo(w[e]) - mean, d1 = E::hi(w[e]) - mean;
+      v = fmaf(d0, d0, fmaf(d1, d1, v));
+    }
   }
   rstd = rsqrtf(v * (1.0f / C) + eps);
 }
@@ -62,20 +64,19 @@ __device__ __forceinline__ void col_stats_mnmajor(const uint8_t* tile, int tok, 
   using E = Elem<T>;
   const uint8_t* base = tile + (tok >> 6) * (C * 128) + (tok & 7) * 2;
   const uint32_t chunk = (tok & 63) >> 3;
-  float vals[C];
-#pragma unroll
-  for (int d = 0; d < C; ++d) {
+  // two passes over shared memory (mean, then squared deviations): no C-float register array
+  auto val = [&](int d) {
     const uint16_t u = *reinterpret_cast<const uint16_t*>(base + d * 128 + ((chunk ^ (d & 7)) << 4));
-    vals[d] = E::lo(static_cast<uint32_t>(u));
-  }
+    return E::lo(static_cast<uint32_t>(u));
+  };
   float s = 0.f;
-#pragma unroll
-  for (int d = 0; d < C; ++d) s += vals[d];
+#pragma unroll 16
+  for (int d = 0; d < C; ++d) s += val(d);
   mean = s * (1.0f / C);
   float v = 0.f;
-#pragma unroll
+#pragma unroll 16
   for (int d = 0; d < C; ++d) {
-    const float dd = vals[d] - mean;
+    const float dd = val(d) - mean;
     v = fmaf(dd, dd, v);
   }
   rstd = rsqrtf(v * (1.0f / C) + eps);
@@ -88,40 +89,53 @@ template <int C>
 struct TmInSmem {
   static constexpr int NOUT = 4 * C;
   static constexpr int TILE = (C / 64) * 16384;
+  // weights per 64-channel K atom, rows reordered by halves: [P(0:C) G(0:C) P(C:2C) G(C:2C)]
   alignas(1024) uint8_t w[(C / 64) * NOUT * 128];
   alignas(1024) uint8_t x[2][TILE];
   float mean[2][128];
   float rstd[2][128];
-  uint64_t bar_w, x_full[2], x_empty[2], st_ready[2], st_free[2], acc_full, acc_empty;
+  alignas(16) float sum_w[NOUT];     // folded LN constants; the G halves pre-scaled by 1/2 (tanh form)
+  alignas(16) float b_const[NOUT];
+  uint64_t bar_w, x_full[2], x_empty[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
 };
 
+// Per 128-token tile the 2C outputs are produced in two halves of C channels: one
+// MMA of N = 2C (P and G of the half) into one of two 2C-column TMEM accumulators,
+// so the MMA of the next half overlaps the epilogue of the current one.
 template <typename T, int C>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     trimul_in_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                      LnGateArgs a) {
   using E = Elem<T>;
   using S = TmInSmem<C>;
-  constexpr int NOUT = S::NOUT;  // P rows [0, 2C), G rows [2C, 4C)
+  constexpr int NOUT = S::NOUT;    // global weight rows: P [0, 2C), G [2C, 4C)
   constexpr int KATOMS = C / 64;
-  constexpr int WBOX = 2 * C > 256 ? 256 : 2 * C;
+  constexpr int NH = 2 * C;        // accumulator columns per half: P(C) | G(C)
+  static_assert(NH <= 256, "one MMA per half");
   extern __shared__ uint8_t smem_raw[];
   S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (a.M + 127) / 128;
+  TOPS_TDECL();
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_w, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.x_full[s], 1);
       mbar_init(&sm.x_empty[s], 1 + 4);
       mbar_init(&sm.st_ready[s], 4);
-      mbar_init(&sm.st_free[s], 4);
+      mbar_init(&sm.st_free[s], 8);
+      mbar_init(&sm.acc_full[s], 1);
+      mbar_init(&sm.acc_empty[s], 8);
     }
-    mbar_init(&sm.acc_full, 1);
-    mbar_init(&sm.acc_empty, 4);
     sm.abort = 0;
     fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < NOUT; i += blockDim.x) {
+    const float sc = i >= 2 * C ? 0.5f : 1.0f;  // sigmoid(g) = 1/2 + tanh(g/2)/2
+    sm.sum_w[i] = a.sum_w[i] * sc;
+    sm.b_const[i] = a.b_const[i] * sc;
   }
   if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
   tc_fence_before();
@@ -134,13 +148,20 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {
       tma_prefetch_desc(&map_x);
       mbar_expect_tx(&sm.bar_w, KATOMS * NOUT * 128);
+      // global row block r0 (C rows of P or G of one half) -> its place in the half-major order
       for (int ka = 0; ka < KATOMS; ++ka)
-        for (int r0 = 0; r0 < NOUT; r0 += WBOX)
-          tma_load_2d(sm.w + ka * NOUT * 128 + r0 * 128, &map_w, &sm.bar_w, ka * 64, r0);
+        for (int r0 = 0; r0 < NOUT; r0 += C) {
+          const int is_g = r0 >= 2 * C, half = (r0 % (2 * C)) / C;
+          const int dst_row = half * NH + is_g * C;
+          tma_load_2d(sm.w + ka * NOUT * 128 + dst_row * 128, &map_w, &sm.bar_w, ka * 64, r0);
+        }
       int it = 0;
       for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
+        TOPS_TCLK(pa);
         if (!mbar_wait(&sm.x_empty[s], ((it >> 1) & 1) ^ 1, abort, 401)) break;
+        TOPS_TCLK(pb);
+        TOPS_TADD(7, pa, pb);
         mbar_expect_tx(&sm.x_full[s], S::TILE);
         for (int ka = 0; ka < KATOMS; ++ka)
           tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.x_full[s], ka * 64, static_cast<int>(tile * 128));
@@ -148,27 +169,34 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr int NCH = 2 * C > 256 ? 256 : 2 * C;  // MMA N per chunk
-      const uint32_t idesc = make_idesc_f16(128, NCH, E::kFmt, false, false);
+      const uint32_t idesc = make_idesc_f16(128, NH, E::kFmt, false, false);
       bool ok = mbar_wait(&sm.bar_w, 0, abort, 402);
       int it = 0;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
+        TOPS_TCLK(ma);
         if (!mbar_wait(&sm.x_full[s], (it >> 1) & 1, abort, 403)) break;
-        if (!mbar_wait(&sm.acc_empty, (it & 1) ^ 1, abort, 404)) break;
-        tc_fence_after();
+        TOPS_TCLK(mb);
+        TOPS_TADD(4, ma, mb);
         const uint32_t xa = smem_u32(sm.x[s]), wa = smem_u32(sm.w);
+        for (int hh = 0; hh < 2; ++hh) {
+          const int u = 2 * it + hh, buf = u & 1;
+          TOPS_TCLK(mc);
+          if (!mbar_wait(&sm.acc_empty[buf], ((u >> 1) & 1) ^ 1, abort, 404)) { ok = false; break; }
+          TOPS_TCLK(md);
+          TOPS_TADD(5, mc, md);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < C / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          const uint32_t woff = (kk >> 2) * (NOUT * 128) + (kk & 3) * 32;
-          const uint64_t ad = make_smem_desc(xa + off, 16, 1024, kSw128);
-#pragma unroll
-          for (int n0 = 0; n0 < NOUT; n0 += NCH)
-            mma_ss(tbase + n0, ad, make_smem_desc(wa + woff + n0 * 128, 16, 1024, kSw128), idesc, kk > 0);
+          for (int kk = 0; kk < C / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            const uint32_t woff = (kk >> 2) * (NOUT * 128) + hh * NH * 128 + (kk & 3) * 32;
+            mma_ss(tbase + buf * 256, make_smem_desc(xa + off, 16, 1024, kSw128),
+                   make_smem_desc(wa + woff, 16, 1024, kSw128), idesc, kk > 0);
+          }
+          mma_commit(&sm.acc_full[buf]);
         }
+        if (!ok) break;
         mma_commit(&sm.x_empty[s]);
-        mma_commit(&sm.acc_full);
       }
     }
   } else if (warp >= 4 && warp < 8) {
@@ -188,44 +216,93 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(&sm.st_ready[s]);
     }
   } else if (warp >= 8) {
-    const int wq = warp - 8;
+    // two epilogue warpgroups split the C channels of each half (a warp reaches only its
+    // own 32 TMEM lanes, so the split is by columns); each lane pairs up with its
+    // neighbour token so that every store is one packed 4-byte pair (k, m..m+1)
+    const int ew = (warp - 8) >> 2;
+    const int wq = warp & 3;
     const int row = wq * 32 + lane;
+    const bool odd = lane & 1;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     T* out = static_cast<T*>(a.out);
+    bool ok = true;
     int it = 0;
-    for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
+      TOPS_TCLK(sa);
       if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 407)) break;
+      TOPS_TCLK(sb2);
+      if (lane == 0) TOPS_TADD(2, sa, sb2);
       const float mean = sm.mean[s][row], rstd = sm.rstd[s][row];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_free[s]);
-      if (!mbar_wait(&sm.acc_full, it & 1, abort, 408)) break;
-      tc_fence_after();
       const long long m = tile * 128 + row;
-      const bool valid = m < a.M;
+      const long long m_even = m & ~1LL;
       float mval = 1.0f;
-      if (a.mask != nullptr && valid) mval = static_cast<float>(static_cast<int8_t>(a.mask[m]));
+      if (a.mask != nullptr && m < a.M) mval = static_cast<float>(static_cast<int8_t>(a.mask[m]));
+      // P' = mval * (rstd p + (-mean rstd sumW + Bc));  G/2 = rstd/2 g + (...)/2 (constants pre-halved)
+      const float rp = rstd * mval, rg = 0.5f * rstd, nm = -mean * rstd;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int u = 2 * it + hh, buf = u & 1;
+        TOPS_TCLK(ea);
+        if (!mbar_wait(&sm.acc_full[buf], (u >> 1) & 1, abort, 408)) { ok = false; break; }
+        TOPS_TCLK(eb);
+        if (lane == 0) TOPS_TADD(0, ea, eb);
+        tc_fence_after();
+        const uint32_t acc = lane_addr + buf * 256;
 #pragma unroll 1
-      for (int k0 = 0; k0 < 2 * C; k0 += 32) {
-        uint32_t p[32], g[32];
-        tmem_ld32(lane_addr + k0, p);
-        tmem_ld32(lane_addr + 2 * C + k0, g);
-        if (valid) {
+        for (int c0 = ew * (C / 2); c0 < (ew + 1) * (C / 2); c0 += 16) {
+          uint32_t pg[32];  // P then G of 16 channels
+          tmem_ld16x2_async(acc + c0, acc + C + c0, pg);
+          tmem_wait_ld32(pg);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int k = k0 + e;
-            const float pv = fmaf(rstd, __uint_as_float(p[e]) - mean * __ldg(a.sum_w + k), __ldg(a.b_const + k));
-            const float gv = fmaf(rstd, __uint_as_float(g[e]) - mean * __ldg(a.sum_w + 2 * C + k),
-                                  __ldg(a.b_const + 2 * C + k));
-            out[static_cast<long long>(k) * a.M + m] = E::from_f(sigmoid_fast(gv) * pv * mval);
+          for (int sub = 0; sub < 16; sub += 8) {
+            // 4 x 8 constants of these channels as 8 broadcast 16-byte shared loads
+            const int kc = hh * C + c0 + sub;
+            float cw[4][8];
+            const float* src[4] = {sm.sum_w + kc, sm.b_const + kc, sm.sum_w + 2 * C + kc, sm.b_const + 2 * C + kc};
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const float4 f = reinterpret_cast<const float4*>(src[q])[i];
+                cw[q][4 * i] = f.x;
+                cw[q][4 * i + 1] = f.y;
+                cw[q][4 * i + 2] = f.z;
+                cw[q][4 * i + 3] = f.w;
+              }
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              float v[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int i = e + h;
+                const float pv = fmaf(rp, __uint_as_float(pg[sub + i]), mval * fmaf(nm, cw[0][i], cw[1][i]));
+                const float gh = fmaf(rg, __uint_as_float(pg[16 + sub + i]), fmaf(nm, cw[2][i], cw[3][i]));
+                v[h] = fmaf(0.5f, tanh_approx(gh), 0.5f) * pv;
+              }
+              // even lane: stores channel k for tokens (m, m+1); odd lane: channel k+1 for (m-1, m)
+              const float other = __shfl_xor_sync(0xffffffffu, odd ? v[0] : v[1], 1);
+              const uint32_t pk = odd ? E::pack2(other, v[1]) : E::pack2(v[0], other);
+              const int k = kc + e + (odd ? 1 : 0);
+              if (m_even < a.M) {
+                if (m_even + 1 < a.M)
+                  *reinterpret_cast<uint32_t*>(out + static_cast<long long>(k) * a.M + m_even) = pk;
+                else
+                  out[static_cast<long long>(k) * a.M + m_even] = E::from_f(odd ? other : v[0]);
+              }
+            }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+        TOPS_TCLK(ec);
+        if (lane == 0) TOPS_TADD(1, eb, ec);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty);
     }
   }
+  TOPS_TFLUSH();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tbase, 512);
@@ -404,13 +481,15 @@ struct TmOutSmem {
   alignas(1024) uint8_t y[2][TILE];                 // MN-major: two 64-token halves x C rows
   alignas(1024) uint8_t x[2][TILE];                 // K-major
   float st[2][4][128];                              // mean_y, rstd_y, mean_x, rstd_x
+  alignas(16) float sum_w[2 * C];                   // folded LN constants (p_out | g_out)
+  alignas(16) float b_const[2 * C];
   uint64_t bar_w, in_full[2], in_empty[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
 };
 
 template <typename T, int C>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     trimul_out_kernel(const __grid_constant__ CUtensorMap map_y, const __grid_constant__ CUtensorMap map_x,
                       const __grid_constant__ CUtensorMap map_w, LnGateArgs a) {
   using E = Elem<T>;
@@ -426,12 +505,17 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&sm.in_full[s], 1);
       mbar_init(&sm.in_empty[s], 1 + 4);
       mbar_init(&sm.st_ready[s], 4);
-      mbar_init(&sm.st_free[s], 4);
+      mbar_init(&sm.st_free[s], 8);
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 4);
+      mbar_init(&sm.acc_empty[s], 8);
     }
     sm.abort = 0;
     fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) {
+    const float sc = i >= C ? 0.5f : 1.0f;  // G half pre-scaled for the tanh form of the sigmoid
+    sm.sum_w[i] = a.sum_w[i] * sc;
+    sm.b_const[i] = a.b_const[i] * sc;
   }
   if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
   tc_fence_before();
@@ -503,7 +587,9 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(&sm.st_ready[s]);
     }
   } else if (warp >= 8) {
-    const int wq = warp - 8;
+    // two epilogue warpgroups split the C output columns of every tile
+    const int ew = (warp - 8) >> 2;
+    const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     int it = 0;
@@ -518,45 +604,64 @@ __global__ void __launch_bounds__(384, 1)
       const long long m = tile * 128 + row;
       T* dst = static_cast<T*>(a.out) + m * C;
       const T* res = a.residual != nullptr ? static_cast<const T*>(a.residual) + m * C : nullptr;
-#pragma unroll 1
-      for (int c0 = 0; c0 < C; c0 += 32) {
-        uint32_t p[32], g[32];
-        tmem_ld32(lane_addr + s * 256 + c0, p);
-        tmem_ld32(lane_addr + s * 256 + C + c0, g);
+      const float nmy = -my * ry, nmx = -mx * rx, rxh = 0.5f * rx;
+      const uint32_t acc = lane_addr + s * 256;
+      // chunk loads (P then G of 16 columns) one chunk ahead of the math
+      uint32_t pg[32], nxt[32];
+      tmem_ld16x2_async(acc + ew * (C / 2), acc + C + ew * (C / 2), pg);
+      tmem_wait_ld32(pg);
+      for (int c0 = ew * (C / 2); c0 < (ew + 1) * (C / 2); c0 += 16) {
+        const bool more = c0 + 16 < (ew + 1) * (C / 2);
+        if (more) tmem_ld16x2_async(acc + c0 + 16, acc + C + c0 + 16, nxt);
         if (m < a.M) {
-          uint32_t rs[16];
-          if (res != nullptr) {
-            const uint4* r4 = reinterpret_cast<const uint4*>(res + c0);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 u = r4[q];
-              rs[4 * q] = u.x;
-              rs[4 * q + 1] = u.y;
-              rs[4 * q + 2] = u.z;
-              rs[4 * q + 3] = u.w;
-            }
-          }
-          uint32_t o[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float v[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int c = c0 + 2 * e + h;
-              const float pv = fmaf(ry, __uint_as_float(p[2 * e + h]) - my * __ldg(a.sum_w + c), __ldg(a.b_const + c));
-              const float gv =
-                  fmaf(rx, __uint_as_float(g[2 * e + h]) - mx * __ldg(a.sum_w + C + c), __ldg(a.b_const + C + c));
-              v[h] = sigmoid_fast(gv) * pv;
-            }
+          for (int sub = 0; sub < 16; sub += 8) {
+            const int cc = c0 + sub;
+            uint32_t rs[4];
             if (res != nullptr) {
-              v[0] += E::lo(rs[e]);
-              v[1] += E::hi(rs[e]);
+              const uint4 u = *reinterpret_cast<const uint4*>(res + cc);
+              rs[0] = u.x;
+              rs[1] = u.y;
+              rs[2] = u.z;
+              rs[3] = u.w;
             }
-            o[e] = E::pack2(v[0], v[1]);
-          }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+            float cw[4][8];
+            const float* src[4] = {sm.sum_w + cc, sm.b_const + cc, sm.sum_w + C + cc, sm.b_const + C + cc};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) d4[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const float4 f = reinterpret_cast<const float4*>(src[q])[i];
+                cw[q][4 * i] = f.x;
+                cw[q][4 * i + 1] = f.y;
+                cw[q][4 * i + 2] = f.z;
+                cw[q][4 * i + 3] = f.w;
+              }
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float v[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int i = 2 * e + h;
+                const float pv = fmaf(ry, __uint_as_float(pg[sub + i]), fmaf(nmy, cw[0][i], cw[1][i]));
+                // G constants pre-halved: sigmoid(g) = 1/2 + tanh(g/2)/2
+                const float gh = fmaf(rxh, __uint_as_float(pg[16 + sub + i]), fmaf(nmx, cw[2][i], cw[3][i]));
+                v[h] = fmaf(0.5f, tanh_approx(gh), 0.5f) * pv;
+              }
+              if (res != nullptr) {
+                v[0] += E::lo(rs[e]);
+                v[1] += E::hi(rs[e]);
+              }
+              o[e] = E::pack2(v[0], v[1]);
+            }
+            *reinterpret_cast<uint4*>(dst + cc) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        if (more) {
+          tmem_wait_ld32(nxt);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pg[i] = nxt[i];
         }
       }
       tc_fence_before();
