@@ -416,9 +416,9 @@ def main():
             cms, sample = cpu_oracle_ms(inp, N, threads)
             cpu = {"value": cms, "unit": "ms", "cores": threads, "kind": "port", "sample": sample}
         # DRAM bytes per attention launch from ncu at N=1024 (profiles/
-        # attn_kernel_triangle_attention_n1024.md: 823 MB read + 256 MB written), scaled by
+        # attn_kernel_triangle_attention_n1024.md: 822.8 MB read + 254.1 MB written), scaled by
         # rows x keys (n * N) — the kernel streams Q/K/V once and writes O once.
-        traffic = 1.0791e9 * (n * N) / (1024 * 1024)
+        traffic = 1.0769e9 * (n * N) / (1024 * 1024)
         line = {
             "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)",
             "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
