@@ -59,7 +59,7 @@ int launch_proj(int dtype, const void* x, const void* w, const ProjArgs& args, c
   set_smem(kern, smem);
   const int tiles = args.trans ? args.R * ((args.Nk + 127) / 128) : (args.T + 127) / 128;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, 384, smem, st>>>(mx, mw, args);
+  kern<<<grid, 512, smem, st>>>(mx, mw, args);
   return launch_status();
 }
 

@@ -17,7 +17,7 @@
 // One GEMM per 128-token tile: x~ (128 x C, K-major, SW128) times the resident
 // concatenated weight Wcat (NOUT x C, K-major, SW128) into a TMEM accumulator of
 // NOUT fp32 columns. Warp roles: w0 TMA producer, w1 MMA issuer, w4-7 LayerNorm
-// (in place in shared memory), w8-11 epilogue (TMEM -> global).
+// (in place in shared memory), w8-15 epilogue (TMEM -> global; two warpgroups, half the heads each).
 #include "sm100.cuh"
 
 namespace tops {
@@ -80,6 +80,8 @@ struct ProjSmem {
   using Cfg = ProjCfg<C, HAS_BP>;
   alignas(1024) uint8_t w[Cfg::WBYTES];
   alignas(1024) uint8_t x[2][Cfg::XSTAGE];
+  alignas(16) float ln_w[C];
+  alignas(16) float ln_b[C];
   uint64_t bar_w;
   uint64_t bar_x_full[2];
   uint64_t bar_x_ready[2];
@@ -91,7 +93,7 @@ struct ProjSmem {
 };
 
 template <typename T, int C, int D, bool HAS_LN, bool HAS_BP>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     proj_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, ProjArgs a) {
   using Cfg = ProjCfg<C, HAS_BP>;
   using E = Elem<T>;
@@ -109,10 +111,15 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&sm.bar_x_empty[s], 1);
     }
     mbar_init(&sm.bar_acc_full, 1);
-    mbar_init(&sm.bar_acc_empty, 4);
+    mbar_init(&sm.bar_acc_empty, 8);
     sm.abort = 0;
     fence_mbar_init();
   }
+  if (HAS_LN)
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+      sm.ln_w[i] = a.ln_w[i];
+      sm.ln_b[i] = a.ln_b[i];
+    }
   if (warp == 1) tmem_alloc(&sm.tmem_base, Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -185,48 +192,51 @@ __global__ void __launch_bounds__(384, 1)
         const int s = it & 1;
         if (!mbar_wait(&sm.bar_x_full[s], (it >> 1) & 1, abort, 105)) break;
         uint8_t* xs = sm.x[s];
-        uint32_t pk[C / 2];  // the row, packed pairs (halves the register footprint of a float copy)
+        // two statistics passes and one normalising pass over the row's 16-byte chunks
+        // (no C-wide register array)
+        auto chunk_ptr = [&](int i) { return xs + (i >> 3) * 16384 + sw128_off(row, i & 7); };
+        float sum = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < C / 8; ++i) {
+          const uint4 u = *reinterpret_cast<const uint4*>(chunk_ptr(i));
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int ka = 0; ka < Cfg::KATOMS; ++ka)
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const uint4 u = *reinterpret_cast<const uint4*>(xs + ka * 16384 + sw128_off(row, ch));
-            const int b = ka * 32 + ch * 4;
-            pk[b] = u.x;
-            pk[b + 1] = u.y;
-            pk[b + 2] = u.z;
-            pk[b + 3] = u.w;
-          }
-        float mean = 0.f;
-#pragma unroll
-        for (int c = 0; c < C / 2; ++c) mean += E::lo(pk[c]) + E::hi(pk[c]);
-        mean *= (1.0f / C);
+          for (int e = 0; e < 4; ++e) sum += E::lo(w[e]) + E::hi(w[e]);
+        }
+        const float mean = sum * (1.0f / C);
         float var = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < C / 8; ++i) {
+          const uint4 u = *reinterpret_cast<const uint4*>(chunk_ptr(i));
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int c = 0; c < C / 2; ++c) {
-          const float d0 = E::lo(pk[c]) - mean, d1 = E::hi(pk[c]) - mean;
-          var = fmaf(d0, d0, fmaf(d1, d1, var));
+          for (int e = 0; e < 4; ++e) {
+            const float d0 = E::lo(w[e]) - mean, d1 = E::hi(w[e]) - mean;
+            var = fmaf(d0, d0, fmaf(d1, d1, var));
+          }
         }
         const float rstd = rsqrtf(var * (1.0f / C) + a.eps);
         bool tvalid;
         const long long tok = proj_token(a, tile, row, tvalid);
         T* xo = a.xln_out != nullptr && tvalid ? static_cast<T*>(a.xln_out) + tok * C : nullptr;
+#pragma unroll 2
+        for (int i = 0; i < C / 8; ++i) {
+          uint8_t* cp = chunk_ptr(i);
+          const uint4 u = *reinterpret_cast<const uint4*>(cp);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          const float4 g0 = reinterpret_cast<const float4*>(sm.ln_w)[2 * i], g1 = reinterpret_cast<const float4*>(sm.ln_w)[2 * i + 1];
+          const float4 b0 = reinterpret_cast<const float4*>(sm.ln_b)[2 * i], b1 = reinterpret_cast<const float4*>(sm.ln_b)[2 * i + 1];
+          const float gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          uint32_t w4[4];
 #pragma unroll
-        for (int ka = 0; ka < Cfg::KATOMS; ++ka)
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c0 = ka * 64 + ch * 8 + 2 * e;
-              const uint32_t pv = pk[c0 >> 1];
-              w4[e] = E::pack2(fmaf((E::lo(pv) - mean) * rstd, __ldg(a.ln_w + c0), __ldg(a.ln_b + c0)),
-                               fmaf((E::hi(pv) - mean) * rstd, __ldg(a.ln_w + c0 + 1), __ldg(a.ln_b + c0 + 1)));
-            }
-            const uint4 u = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            *reinterpret_cast<uint4*>(xs + ka * 16384 + sw128_off(row, ch)) = u;
-            if (xo != nullptr) *reinterpret_cast<uint4*>(xo + ka * 64 + ch * 8) = u;
-          }
+          for (int e = 0; e < 4; ++e)
+            w4[e] = E::pack2(fmaf((E::lo(w[e]) - mean) * rstd, gw[2 * e], bw[2 * e]),
+                             fmaf((E::hi(w[e]) - mean) * rstd, gw[2 * e + 1], bw[2 * e + 1]));
+          const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          *reinterpret_cast<uint4*>(cp) = o;
+          if (xo != nullptr) *reinterpret_cast<uint4*>(xo + i * 8) = o;
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.bar_x_ready[s]);
@@ -234,7 +244,10 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp >= 8) {
     // ---------------- epilogue (w8-11) ----------------
-    const int wq = warp - 8;
+    // two epilogue warpgroups: heads [0, H/2) and [H/2, H); the first also writes the
+    // bias and mask rows
+    const int ew = (warp - 8) >> 2;
+    const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     float bz[H];
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(384, 1)
       if (a.mask != nullptr && valid) mval = a.mask[static_cast<long long>(ri) * a.Nk + kpos] ? 1.0f : 0.0f;
       uint32_t r[32];
 #pragma unroll
-      for (int h = 0; h < H; ++h) {
+      for (int h = ew * (H / 2); h < (ew + 1) * (H / 2); ++h) {
         const size_t qk_off = ((static_cast<size_t>(ri) * H + h) * a.Nk + kpos) * D;
         // Q
         if (D == 32) tmem_ld32(lane_addr + h * D, r); else tmem_ld16(lane_addr + h * D, r);
@@ -285,7 +298,7 @@ __global__ void __launch_bounds__(384, 1)
           for (int d = 0; d < D; ++d) dst[static_cast<size_t>(d) * a.Nkp] = __float2half_rn(__uint_as_float(r[d]) * mval);
         }
       }
-      if (HAS_BP) {
+      if (HAS_BP && ew == 0) {
         tmem_ld16(lane_addr + 3 * C, r);
         if (valid)
 #pragma unroll
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(384, 1)
             static_cast<__half*>(a.bp)[(static_cast<size_t>(h) * a.R + ri) * a.Nkp + kpos] =
                 __float2half_rn((__uint_as_float(r[h]) + bz[h]) * 1.4426950408889634f);
       }
-      if (valid) static_cast<__half*>(a.maskf)[static_cast<size_t>(ri) * a.Nkp + kpos] = __float2half_rn(mval);
+      if (valid && ew == 0) static_cast<__half*>(a.maskf)[static_cast<size_t>(ri) * a.Nkp + kpos] = __float2half_rn(mval);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.bar_acc_empty);
