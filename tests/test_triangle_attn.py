@@ -96,3 +96,24 @@ def test_lowlevel_triangle_attn_forward(device):
     o = tops.triangle_attn.fused_gate_forward(out.view(130, 130, H, D), X_ln, W_pg, W_po)
     ref = oracle.triangle_attention(*args, scale=0.2, mask=mask)
     assert_parity(o, ref, torch.bfloat16, "low-level")
+
+
+def test_host_pipeline_matches_forward(device):
+    """HostPipeline (pinned host tensors, slab-streamed copies, calls overlapping) gives the
+    device forward's result, including a fully masked row, over back-to-back calls."""
+    N, H, D, C = 256, 4, 32, 128
+    args, mask = _inputs(N, H, D, C, torch.bfloat16, device, general=True, masked=True)
+    (X, W_ln, B_ln, WQ, WK, WV, W_pz, B_pz, W_pg, _, W_po, _, H, D) = args
+    mask[5] = False
+    pre = tops.triangle_attn.precompute(W_ln, B_ln, WQ, WK, WV, W_pz, B_pz, H, D)
+    kw = dict(scale=D**-0.5, W_proj_g=W_pg, W_proj_o=W_po)
+    pipe = tops.triangle_attn.HostPipeline(pre, slabs=4, **kw)
+    X2 = rnd(N, N, C, dtype=torch.bfloat16, device=device, seed=77)
+    outs = []
+    for Xi in (X, X2, X):
+        outs.append(pipe(Xi.cpu().pin_memory(), mask.cpu().pin_memory()))
+    pipe.wait()
+    torch.cuda.synchronize()
+    for Xi, o in zip((X, X2, X), outs):
+        ref = tops.triangle_attn.forward(Xi, pre, mask=mask, B_proj_g=None, B_proj_o=None, **kw)
+        assert torch.equal(o, ref.cpu()), (o.float() - ref.cpu().float()).abs().max()

@@ -1,0 +1,140 @@
+"""Triangle attention on host (pinned) tensors with the copies overlapped.
+
+A caller whose pair tensor lives in host memory pays one host->device copy of X
+and one device->host copy of the result per call (2 x 1 GiB at N = 2048, C = 128,
+about 20 ms each over PCIe). ``HostPipeline`` hides most of it:
+
+* within a call, X arrives in row slabs on a copy stream and each slab is
+  projected (LN + Q/K/V/bias, ``tops_triangle_attn_project``) as soon as it lands;
+  after the last slab the bias slabs are assembled (every row's attention needs the
+  whole shared bias), then attention + gate run slab by slab and each finished slab
+  leaves on a second copy stream while the next one computes;
+* across calls nothing synchronises, so the host->device copy of call t+1 runs
+  while call t computes and copies its result back (PCIe is full duplex).
+
+Device buffers are allocated once per (N, C, H, D, dtype) and reused; events keep
+each buffer from being overwritten before its previous reader has finished. The
+work of a call is complete when ``wait(stream)`` returns on a stream (it makes that
+stream wait) or after ``torch.cuda.synchronize()``.
+
+No counterpart in the reference (it takes device tensors only); the per-slab work is
+the same kernels as ``module.forward``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from .kernel import _mask_u8, gate_forward
+
+
+class HostPipeline:
+    def __init__(self, pre, *, W_proj_g, W_proj_o, scale=1.0, eps=1e-5, slabs=8):
+        self.pre = pre
+        self.Wg, self.Wo = W_proj_g, W_proj_o
+        self.scale, self.eps, self.slabs = float(scale), float(eps), int(slabs)
+        self._key = None
+
+    def _setup(self, N, C, dtype, dev):
+        H, D = self.pre["H"], self.pre["D"]
+        key = (N, C, H, D, dtype, dev)
+        if key == self._key:
+            return
+        assert N % self.slabs == 0, f"N={N} must be divisible by slabs={self.slabs}"
+        nkp = (N + 7) // 8 * 8
+        R = N // self.slabs
+        f16 = torch.float16
+        self.N, self.C, self.R, self.nkp, self.H, self.D = N, C, R, nkp, H, D
+        self.x = torch.empty(N, N, C, dtype=dtype, device=dev)
+        self.m = torch.empty(N, N, dtype=torch.uint8, device=dev)
+        self.xln = torch.empty(N, N, C, dtype=dtype, device=dev)
+        self.q = torch.empty(N, H, N, D, dtype=f16, device=dev)
+        self.k = torch.empty(N, H, N, D, dtype=f16, device=dev)
+        self.vt = torch.empty(N, H, D, nkp, dtype=f16, device=dev)
+        self.maskf = torch.empty(N, nkp, dtype=f16, device=dev)
+        self.bias_slab = torch.empty(self.slabs, H, R, nkp, dtype=f16, device=dev)
+        self.bias = torch.empty(H, N, nkp, dtype=f16, device=dev)
+        self.o = torch.empty(N, N, H * D, dtype=dtype, device=dev)
+        self.out = torch.empty(N, N, C, dtype=dtype, device=dev)
+        self.w = self.pre["W_qkvz"] if self.pre["W_qkvz"].dtype == dtype else self.pre["W_qkvz"].to(dtype)
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        ev = lambda: [torch.cuda.Event() for _ in range(self.slabs)]  # noqa: E731
+        self.ev_in, self.ev_proj, self.ev_gate, self.ev_out = ev(), ev(), ev(), ev()
+        self.started = False
+        self._key = key
+
+    def __call__(self, X_host, mask_host=None, out_host=None):
+        """Enqueue one forward of X_host (N, N, C) pinned; the result lands in out_host
+        (allocated pinned if None, returned). mask_host: (N, N) bool/int, pinned, or None."""
+        N, _, C = X_host.shape
+        dev = torch.device("cuda", torch.cuda.current_device())
+        _lib.require_cuda(torch.empty(0, device=dev))
+        self._setup(N, C, X_host.dtype, dev)
+        if out_host is None:
+            out_host = torch.empty(N, N, C, dtype=X_host.dtype).pin_memory()
+        dead = None
+        if mask_host is not None:
+            mask_host = mask_host.reshape(N, N)
+            if mask_host.dtype == torch.bool:
+                mask_host = mask_host.view(torch.uint8)  # same bytes, still pinned
+            elif mask_host.dtype != torch.uint8:
+                mask_host = _mask_u8(mask_host, (N, N))
+            # fully masked rows (the reference's -1e9 turns them into a uniform average
+            # over all keys; the kernel drops masked keys): found on the host, no sync
+            dead = (~mask_host.bool().any(dim=1)).nonzero().flatten()
+        compute = torch.cuda.current_stream(dev)
+        dt = _lib.dtype_code(X_host.dtype)
+        R, H, D, nkp = self.R, self.H, self.D, self.nkp
+        st = compute.cuda_stream
+        pre = self.pre
+        # --- stage A: slabs in, projected as they land
+        for i in range(self.slabs):
+            r0, r1 = i * R, (i + 1) * R
+            with torch.cuda.stream(self.h2d):
+                if self.started:
+                    self.h2d.wait_event(self.ev_proj[i])  # the previous call's projection read this slab
+                self.x[r0:r1].copy_(X_host[r0:r1], non_blocking=True)
+                if mask_host is not None:
+                    self.m[r0:r1].copy_(mask_host[r0:r1], non_blocking=True)
+                self.ev_in[i].record(self.h2d)
+            compute.wait_event(self.ev_in[i])
+            _lib.call("tops_triangle_attn_project", dt, R, N, C, H, D, self.x[r0].data_ptr(), 1,
+                      pre["ln_w32"].data_ptr(), pre["ln_b32"].data_ptr(), self.w.data_ptr(), pre["BZ"].data_ptr(),
+                      None if mask_host is None else self.m[r0].data_ptr(), self.scale, self.eps,
+                      self.xln[r0].data_ptr(), self.q[r0].data_ptr(), self.k[r0].data_ptr(), self.vt[r0].data_ptr(),
+                      self.maskf[r0].data_ptr(), self.bias_slab[i].data_ptr(), st)
+            self.ev_proj[i].record(compute)
+        # the shared bias, [H][N][Np], from the slabs' [H][R][Np] blocks
+        self.bias.view(H, self.slabs, R, nkp).copy_(self.bias_slab.permute(1, 0, 2, 3))
+        # --- stage B: attention + gate per slab, each slab out while the next computes
+        for i in range(self.slabs):
+            r0, r1 = i * R, (i + 1) * R
+            _lib.call("tops_triangle_attn_attend", dt, R, N, H, D, self.q[r0].data_ptr(), self.k[r0].data_ptr(),
+                      self.vt[r0].data_ptr(), self.maskf[r0].data_ptr(), self.bias.data_ptr(), self.o[r0].data_ptr(),
+                      st)
+            if dead is not None:
+                rows = dead[(dead >= r0) & (dead < r1)]
+                if rows.numel():
+                    idx = rows.to(dev, non_blocking=True)
+                    mv = (self.xln[idx].float().mean(dim=1) @ self.w[2 * H * D:3 * H * D].t().float())
+                    self.o[idx] = mv.to(self.o.dtype)[:, None, :].expand(-1, N, -1)
+            if self.started:
+                compute.wait_event(self.ev_out[i])  # the previous call's copy-out of this slab
+            gate_forward(self.o[r0:r1].view(R * N, H * D), self.xln[r0:r1].view(R * N, C), self.Wg, self.Wo,
+                         out=self.out[r0:r1].view(R * N, C))
+            self.ev_gate[i].record(compute)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.ev_gate[i])
+                out_host[r0:r1].copy_(self.out[r0:r1], non_blocking=True)
+                self.ev_out[i].record(self.d2h)
+        self.started = True
+        return out_host
+
+    def wait(self, stream=None):
+        """Make ``stream`` (default: the current one) wait for every enqueued copy-out."""
+        stream = torch.cuda.current_stream() if stream is None else stream
+        if self.started:
+            for e in self.ev_out:
+                stream.wait_event(e)
