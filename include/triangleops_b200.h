@@ -191,6 +191,20 @@ int tops_apb_forward_noalloc(int dtype, int64_t M, int64_t C, int64_t Cz, int64_
                              void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Workspace sizes (host-only, no device work; no counterpart in the reference,
+ * whose temporaries torch allocates inside
+ * triangle_attn/kernel.py:300-301,326). Each writes byte counts in the order listed
+ * and validates the shape like the entry point that takes the workspaces. */
+
+/* bytes[6] = xln, q, k, vt, maskf, bias for R projected rows of an N x N problem. */
+int tops_triangle_attn_workspace_bytes(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
+                                       int64_t* bytes);
+/* bytes[2] = ab [2C][B*L*L], y [C][B*L*L]. */
+int tops_trimul_workspace_bytes(int dtype, int64_t B, int64_t L, int64_t C, int64_t* bytes);
+/* bytes[5] = q, k, vt, maskf, bias for query rows Mq of M tokens. */
+int tops_apb_workspace_bytes(int64_t M, int64_t Mq, int64_t H, int64_t D, int64_t* bytes);
+
+/* ---------------------------------------------------------------------------
  * fp32 IO path (CUDA cores). The reference admits fp32 IO for all three ops
  * (_common/dtype.py:7-19) and then runs its Triton kernels in fp32; these four
  * generic kernels are what the package composes each op's fp32 forward from

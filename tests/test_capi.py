@@ -80,3 +80,28 @@ def test_drop_in_import_name():
     assert tm.precompute is triangle_ops.triangle_mul.precompute
     for name in ("triangle_attention", "triangle_multiplicative_update", "attention_pair_bias"):
         assert hasattr(triangle_ops, name)
+
+
+def test_workspace_bytes_match_the_python_layer():
+    """The host-only size queries agree with the workspaces the Python layer allocates
+    (triangle_attn/kernel.py, triangle_mul/kernel.py, attn_pair_bias/kernel.py) and
+    reject bad shapes; they need no GPU."""
+    lib = ctypes.CDLL(_build.build())
+    I64 = ctypes.c_int64
+    out = (I64 * 6)()
+    N, C, H, D = 130, 128, 4, 32
+    np_ = (N + 7) // 8 * 8
+    assert lib.tops_triangle_attn_workspace_bytes(1, I64(N), I64(N), I64(C), I64(H), I64(D), out) == 0
+    assert list(out) == [N * N * C * 2, N * H * N * D * 2, N * H * N * D * 2, N * H * D * np_ * 2, N * np_ * 2,
+                         H * N * np_ * 2]
+    assert lib.tops_triangle_attn_workspace_bytes(1, I64(N + 1), I64(N), I64(C), I64(H), I64(D), out) == _lib.ERR_SHAPE
+    assert lib.tops_triangle_attn_workspace_bytes(2, I64(N), I64(N), I64(C), I64(H), I64(D), out) == _lib.ERR_DTYPE
+    B, L = 2, 64
+    assert lib.tops_trimul_workspace_bytes(0, I64(B), I64(L), I64(C), out) == 0
+    assert list(out)[:2] == [2 * C * B * L * L * 2, C * B * L * L * 2]
+    M, Mq = 200, 100
+    mp = (M + 7) // 8 * 8
+    assert lib.tops_apb_workspace_bytes(I64(M), I64(Mq), I64(H), I64(D), out) == 0
+    assert list(out)[:5] == [H * M * D * 2, H * M * D * 2, H * D * mp * 2, mp * 2, H * Mq * mp * 4]
+    assert lib.tops_apb_workspace_bytes(I64(M), I64(M + 1), I64(H), I64(D), out) == _lib.ERR_SHAPE
+    assert lib.tops_apb_workspace_bytes(I64(M), I64(M), I64(H), I64(D), None) == _lib.ERR_ARG
