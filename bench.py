@@ -15,6 +15,8 @@ the shared bias is all-gathered over NCCL (strong scaling: total work fixed).
                path) on the host cores, on a bounded row sample, extrapolated
   ops          (1 GPU only) the other two ops at their configs (3 and 2)
 
+``--impl reference-gpu`` times the reference's own Triton kernels (installed under
+baseline/_ref) on the GPU as a second comparator, with the output difference to ours.
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 oracle port, all host threads) on the same workload and prints its line.
 """
@@ -167,6 +169,99 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args):
+    """Second comparator (not the driver's reference arm): the reference's own Triton
+    kernels, installed unmodified under baseline/_ref, timed on this B200 through its
+    public API (precompute once, forward per call) on the same inputs, plus the
+    largest difference between its output and ours on those inputs."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "triangle_ops")):
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "baseline/_ref not installed"}), flush=True)
+        return
+    sys.path.insert(0, ref_dir)
+    for k in [k for k in sys.modules if k == "triangle_ops" or k.startswith("triangle_ops.")]:
+        del sys.modules[k]
+    import triangle_ops as ref  # the reference package, not the drop-in alias
+
+    assert os.path.abspath(ref.__file__).startswith(ref_dir), ref.__file__
+    dev = torch.device("cuda", 0)
+    N = args.n
+    inp = make_inputs(N, dev)
+    scale = 1 / math.sqrt(D)
+    pre = ref.triangle_attn.precompute(inp["W_ln"], inp["B_ln"], inp["WQ"], inp["WK"], inp["WV"], inp["W_proj_z"],
+                                       None, H, D)
+
+    def step():
+        return ref.triangle_attn.forward(inp["X"], pre, mask=inp["mask"], scale=scale, W_proj_g=inp["W_proj_g"],
+                                         B_proj_g=None, W_proj_o=inp["W_proj_o"], B_proj_o=None)
+
+    ms = time_op(step, iters=args.steps, warmup=max(args.warmup, 2))
+    out_ref = step().float()
+    import triangleops_b200 as tops
+
+    ours_pre = tops.triangle_attn.precompute(inp["W_ln"], inp["B_ln"], inp["WQ"], inp["WK"], inp["WV"],
+                                             inp["W_proj_z"], None, H, D)
+    ours = tops.triangle_attn.forward(inp["X"], ours_pre, mask=inp["mask"], scale=scale, W_proj_g=inp["W_proj_g"],
+                                      B_proj_g=None, W_proj_o=inp["W_proj_o"], B_proj_o=None).float()
+    d = (ours - out_ref).abs()
+    cos = torch.nn.functional.cosine_similarity(ours.flatten().double(), out_ref.flatten().double(), dim=0).item()
+    parity = {"max_abs_diff": d.max().item(), "mean_abs_diff": d.mean().item(), "cosine": cos}
+    ops = {}
+    del ours, out_ref, d
+    # config 3: triangle_mul incoming L=2048 with the padded-tail outer-product mask
+    g3 = torch.Generator(device=dev).manual_seed(3)
+    rn3 = lambda *sh, sd=1.0: (torch.randn(*sh, generator=g3, device=dev) * sd).to(torch.bfloat16)  # noqa: E731
+    L = 2048
+    x = rn3(1, L, L, C)
+    v = torch.zeros(L, device=dev)
+    v[:1900] = 1
+    m3 = (v[:, None] * v[None, :])[None]
+    w = [1 + 0.1 * rn3(C), 0.1 * rn3(C), rn3(2 * C, C, sd=C**-0.5), rn3(2 * C, C, sd=C**-0.5), 1 + 0.1 * rn3(C),
+         0.1 * rn3(C), rn3(C, C, sd=C**-0.5), rn3(C, C, sd=C**-0.5)]
+    rp, op_ = ref.triangle_mul.precompute(*w), tops.triangle_mul.precompute(*w)
+    fr = lambda: ref.triangle_mul.forward(x, rp, direction="incoming", mask=m3)  # noqa: E731
+    fo = lambda: tops.triangle_mul.forward(x, op_, direction="incoming", mask=m3)  # noqa: E731
+    rms, oms = time_op(fr, iters=args.steps), time_op(fo, iters=args.steps)
+    a_, b_ = fr().float(), fo().float()
+    ops["triangle_multiplicative_update"] = {
+        "config": "incoming L=2048 C=128 bf16, mask tail 1900", "reference_ms": rms, "ours_ms": oms,
+        "max_abs_diff": (a_ - b_).abs().max().item(),
+        "cosine": torch.nn.functional.cosine_similarity(a_.flatten().double(), b_.flatten().double(), dim=0).item()}
+    del x, a_, b_
+    # config 2 shapes (the reference apb takes no mask: unmasked here)
+    g2 = torch.Generator(device=dev).manual_seed(2)
+    rn2 = lambda *sh, sd=1.0: (torch.randn(*sh, generator=g2, device=dev) * sd)  # noqa: E731
+    M = 1024
+    X2 = torch.nn.functional.layer_norm(rn2(M, C), (C,), 1 + 0.1 * rn2(C), 0.1 * rn2(C)).to(torch.bfloat16)
+    Z = rn2(M, M, C).to(torch.bfloat16)
+    W_ln, B_ln = (1 + 0.1 * rn2(C)).to(torch.bfloat16), (0.1 * rn2(C)).to(torch.bfloat16)
+    Wq, Wk, Wv, Wg, Wo = (rn2(C, C, sd=C**-0.5).to(torch.bfloat16) for _ in range(5))
+    Wz = rn2(H, C, sd=C**-0.5).to(torch.bfloat16).t().contiguous()
+    Bz = torch.zeros(H, device=dev, dtype=torch.bfloat16)  # the reference's precompute needs a tensor here
+    rp = ref.attn_pair_bias.precompute(Wq, Wk, Wv, W_ln, B_ln, Wz, Bz, H, D)
+    op_ = tops.attn_pair_bias.precompute(Wq, Wk, Wv, W_ln, B_ln, Wz, Bz, H, D)
+    kw = dict(scale=1.0, W_proj_g=Wg, B_proj_g=None, W_proj_o=Wo, B_proj_o=None)
+    fr = lambda: ref.attn_pair_bias.forward(X2, Z, rp, **kw)  # noqa: E731
+    fo = lambda: tops.attn_pair_bias.forward(X2, Z, op_, **kw)  # noqa: E731
+    rms, oms = time_op(fr, iters=20), time_op(fo, iters=20)
+    a_, b_ = fr().float(), fo().float()
+    ops["attention_pair_bias"] = {
+        "config": "M=1024 c_s=C_z=128 bf16, no mask", "reference_ms": rms, "ours_ms": oms,
+        "max_abs_diff": (a_ - b_).abs().max().item(),
+        "cosine": torch.nn.functional.cosine_similarity(a_.flatten().double(), b_.flatten().double(), dim=0).item()}
+    line = {"impl": "reference-gpu", "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)",
+            "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "higher_is_better": False,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128 bf16, mask "
+                                   "Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)",
+                       "implementation": "reference Triton kernels (baseline/_ref), unmodified, JIT for sm_100"},
+            "parity_vs_ours": parity, "ops": ops}
+    print(json.dumps(line), flush=True)
+
+
 def time_op(fn, iters=10, warmup=3):
     for _ in range(warmup):
         fn()
@@ -298,13 +393,16 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--n", type=int, default=N_DEF)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ops", action="store_true", help="skip the other two ops")
     ap.add_argument("--profile-op", choices=["triangle_mul", "attn_pair_bias"], default=None,
                     help="run only this op (config 3 / config 2 shapes at --n) for profiling, print its time")
     args = ap.parse_args()
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args)
+        return
     if args.impl == "reference":
         return run_reference(args)
     if args.profile_op:

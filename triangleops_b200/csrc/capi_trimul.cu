@@ -76,7 +76,7 @@ int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, cons
   set_smem(kern, smem);
   const long long tiles = static_cast<long long>((Mi + kCtBM - 1) / kCtBM) * ((L + kCtBN - 1) / kCtBN) * nb;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 256, smem, st>>>(ma, mb, args);
+  kern<<<grid, 384, smem, st>>>(ma, mb, args);
   return launch_status();
 }
 

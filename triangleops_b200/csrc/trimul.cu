@@ -309,14 +309,19 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 // ===========================================================================
-// contraction (per-channel batched GEMM, 128 x 256 tiles, BK = 64, 4 stages)
+// contraction (per-channel batched GEMM, 256 x 256 tiles, BK = 64, 3 stages)
 // ===========================================================================
-constexpr int kCtBM = 128, kCtBN = 256, kCtBK = 64, kCtStages = 4;
+// A 256 x 256 tile is two M=128 MMAs sharing each B tile: 2 x 256 TMEM columns
+// (all of TMEM, one accumulator pair). The larger tile halves the operand bytes per
+// FLOP against 128 x 256, which is what the stage ring can keep in flight from L2;
+// the epilogue (8 warps, one per TMEM lane quarter and row half) is short next to
+// the K loop, so the accumulator is not double-buffered.
+constexpr int kCtBM = 256, kCtBN = 256, kCtBK = 64, kCtStages = 3;
 
 struct CtSmem {
   alignas(1024) uint8_t a[kCtStages][kCtBM * kCtBK * 2];
   alignas(1024) uint8_t b[kCtStages][kCtBN * kCtBK * 2];
-  uint64_t full[kCtStages], empty[kCtStages], acc_full[2], acc_empty[2];
+  uint64_t full[kCtStages], empty[kCtStages], acc_full, acc_empty;
   uint32_t tmem_base;
   int abort;
 };
@@ -329,7 +334,7 @@ struct CtArgs {
 };
 
 template <typename T, bool MN>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     trimul_contract_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            CtArgs a) {
   using E = Elem<T>;
@@ -344,10 +349,8 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 4);
-    }
+    mbar_init(&sm.acc_full, 1);
+    mbar_init(&sm.acc_empty, 8);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -400,14 +403,12 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(kCtBM, kCtBN, E::kFmt, MN, MN);
+      const uint32_t idesc = make_idesc_f16(128, kCtBN, E::kFmt, MN, MN);
       int g = 0, it = 0;
       bool ok = true;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
-        const int acc = it & 1;
-        if (!mbar_wait(&sm.acc_empty[acc], ((it >> 1) & 1) ^ 1, abort, 502)) break;
+        if (!mbar_wait(&sm.acc_empty, (it & 1) ^ 1, abort, 502)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tbase + acc * 256;
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int s = g % kCtStages;
           if (!mbar_wait(&sm.full[s], (g / kCtStages) & 1, abort, 503)) { ok = false; break; }
@@ -415,29 +416,28 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t aa = smem_u32(sm.a[s]), ba = smem_u32(sm.b[s]);
 #pragma unroll
           for (int kk = 0; kk < kCtBK / 16; ++kk) {
-            uint64_t ad, bd;
-            if (!MN) {
-              ad = make_smem_desc(aa + kk * 32, 16, 1024, kSw128);
-              bd = make_smem_desc(ba + kk * 32, 16, 1024, kSw128);
-            } else {
-              ad = make_smem_desc(aa + kk * 2048, 8192, 1024, kSw128);
-              bd = make_smem_desc(ba + kk * 2048, 8192, 1024, kSw128);
+            const uint64_t bd = MN ? make_smem_desc(ba + kk * 2048, 8192, 1024, kSw128)
+                                   : make_smem_desc(ba + kk * 32, 16, 1024, kSw128);
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {  // rows [128m, 128m + 128): 16 KB into the A tile either way
+              const uint64_t ad = MN ? make_smem_desc(aa + m * 16384 + kk * 2048, 8192, 1024, kSw128)
+                                     : make_smem_desc(aa + m * 16384 + kk * 32, 16, 1024, kSw128);
+              mma_ss(tbase + m * 256, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             }
-            mma_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&sm.empty[s]);
         }
-        if (ok) mma_commit(&sm.acc_full[acc]);
+        if (ok) mma_commit(&sm.acc_full);
       }
     }
   } else if (warp >= 4) {
-    const int wq = warp - 4;
-    const int row = wq * 32 + lane;
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    // 8 epilogue warps: row half m = (warp - 4) / 4 (its accumulator), lane quarter warp % 4
+    const int m = (warp - 4) >> 2, wq = warp & 3;
+    const int row = m * 128 + wq * 32 + lane;
+    const uint32_t lane_addr = tbase + m * 256 + (static_cast<uint32_t>(wq * 32) << 16);
     int it = 0;
     for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-      const int acc = it & 1;
-      if (!mbar_wait(&sm.acc_full[acc], (it >> 1) & 1, abort, 504)) break;
+      if (!mbar_wait(&sm.acc_full, it & 1, abort, 504)) break;
       tc_fence_after();
       int bb, i0, j0;
       decode(tile, bb, i0, j0);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < kCtBN; c0 += 32) {
         uint32_t r[32];
-        tmem_ld32(lane_addr + acc * 256 + c0, r);
+        tmem_ld32(lane_addr + c0, r);
         if (i < a.Mi) {
           uint32_t p[16];
 #pragma unroll
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(256, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+      if (lane == 0) mbar_arrive(&sm.acc_empty);
     }
   }
   tc_fence_before();
