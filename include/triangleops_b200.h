@@ -114,7 +114,7 @@ int tops_fused_gate_residual(int dtype, int64_t T, int64_t C, const void* o, con
  * Input phase — replaces triangle_mul/kernel.py:235-279 (input_phase):
  *   ab_out[k][m] = mask[m] * sigmoid(LN(x) g_in^T)[m,k] * (LN(x) p_in^T)[m,k], k < 2C, D-major.
  *   x [M][C]; mask [M] int8 multiplier or NULL; w_in [4C][C] = p_in_c | g_in_c (LN-folded);
- *   sum_in, b_in [4C] fp32 (folded column sums / biases); ab_out [2C][M]. C in {64,128}. */
+ *   sum_in, b_in [4C] fp32 (folded column sums / biases); ab_out [2C][M]. C in {64,128}; M % 8 == 0. */
 int tops_trimul_input_phase(int dtype, int64_t M, int64_t C, const void* x, const uint8_t* mask, const void* w_in,
                             const float* sum_in, const float* b_in, float eps, void* ab_out, void* stream);
 /* Triangular contraction — replaces the torch.einsum of triangle_mul/module.py:70-76.

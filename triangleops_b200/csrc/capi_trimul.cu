@@ -121,6 +121,7 @@ extern "C" int tops_trimul_input_phase(int dtype, int64_t M, int64_t C, const vo
                                        void* ab_out, void* stream) {
   if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
   if (M <= 0 || (C != 128 && C != 64)) return TOPS_ERR_SHAPE;
+  if (M % 8 != 0) return TOPS_ERR_ALIGN;  // D-major rows of ab start 16-byte aligned; token pairs whole
   const void* ptrs[] = {x, w_in, sum_in, b_in, ab_out};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;

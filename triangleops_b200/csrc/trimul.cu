@@ -284,13 +284,9 @@ __global__ void __launch_bounds__(512, 1)
               // even lane: stores channel k for tokens (m, m+1); odd lane: channel k+1 for (m-1, m)
               const float other = __shfl_xor_sync(0xffffffffu, odd ? v[0] : v[1], 1);
               const uint32_t pk = odd ? E::pack2(other, v[1]) : E::pack2(v[0], other);
+              // M is even (the C ABI checks it), so a token pair is either whole or past the end
               const int k = kc + e + (odd ? 1 : 0);
-              if (m_even < a.M) {
-                if (m_even + 1 < a.M)
-                  *reinterpret_cast<uint32_t*>(out + static_cast<long long>(k) * a.M + m_even) = pk;
-                else
-                  out[static_cast<long long>(k) * a.M + m_even] = E::from_f(odd ? other : v[0]);
-              }
+              if (m < a.M) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(k) * a.M + m_even) = pk;
             }
           }
         }
