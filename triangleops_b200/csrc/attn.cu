@@ -39,8 +39,8 @@
 // max grows by more than 2^8). The per-element work runs on f16 pairs: S + bias is
 // rounded to f16 (relative error 2^-11, well below the 2^-8 rounding the 16-bit Q
 // and K already put into S), the row max is a pairwise tree, and
-// P = 2^(x - m), 3/5 of the pairs on the MUFU (ex2.approx.f16x2, which issues twice
-// on the XU pipe) and 2/5 by a polynomial on the FMA pipe (ex2_poly_f16x2), so that
+// P = 2^(x - m), 2/3 of the pairs on the MUFU (ex2.approx.f16x2, which issues twice
+// on the XU pipe) and 1/3 by a polynomial on the FMA pipe (ex2_poly_f16x2), so that
 // neither pipe alone bounds the step; V^T and the mask row are f16 for the PV MMA.
 #include "sm100.cuh"
 
@@ -51,7 +51,7 @@ namespace tops {
 #endif
 constexpr bool kPolyExp = TOPS_POLY_EXP != 0;
 #ifndef TOPS_POLY_PICK
-#define TOPS_POLY_PICK(c) ((c) % 5 == 1 || (c) % 5 == 3)  // pairs whose 2^x takes the polynomial
+#define TOPS_POLY_PICK(c) ((c) % 3 == 1)  // pairs whose 2^x takes the polynomial (11 of 32)
 #endif
 #ifndef TOPS_ATTN_SMEM_KB
 #define TOPS_ATTN_SMEM_KB 200  // operand budget (Q tiles + stages); the B200 allows 227 KB per CTA
@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, TQ, BF32>::THREADS, 1)
           }
         }
         const __half2 mh = __float2half2_rn(m_use);  // exact: m_use is an f16 value
-        // 2/5 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
+        // about 1/3 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
         // the XU pipe (2 issues per f16 pair) and the FMA pipe then finish together.
         uint32_t pk[32];
 #pragma unroll
