@@ -17,7 +17,7 @@ int launch_trimul_in(int dtype, const void* x, const void* w, const LnGateArgs& 
   set_smem(kern, smem);
   const long long tiles = (args.M + 127) / 128;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 512, smem, st>>>(mx, mw, args);
+  kern<<<grid, 256 + 128 * kInEpiWG, smem, st>>>(mx, mw, args);
   return launch_status();
 }
 

@@ -101,11 +101,14 @@ struct TmInSmem {
   int abort;
 };
 
+// epilogue warpgroups of the input phase (each takes C / kInEpiWG channels of a half)
+constexpr int kInEpiWG = 4;
+
 // Per 128-token tile the 2C outputs are produced in two halves of C channels: one
 // MMA of N = 2C (P and G of the half) into one of two 2C-column TMEM accumulators,
 // so the MMA of the next half overlaps the epilogue of the current one.
 template <typename T, int C>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
     trimul_in_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                      LnGateArgs a) {
   using E = Elem<T>;
@@ -125,9 +128,9 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(&sm.x_full[s], 1);
       mbar_init(&sm.x_empty[s], 1 + 4);
       mbar_init(&sm.st_ready[s], 4);
-      mbar_init(&sm.st_free[s], 8);
+      mbar_init(&sm.st_free[s], 4 * kInEpiWG);
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 8);
+      mbar_init(&sm.acc_empty[s], 4 * kInEpiWG);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -216,8 +219,8 @@ __global__ void __launch_bounds__(512, 1)
       if (lane == 0) mbar_arrive(&sm.st_ready[s]);
     }
   } else if (warp >= 8) {
-    // two epilogue warpgroups split the C channels of each half (a warp reaches only its
-    // own 32 TMEM lanes, so the split is by columns); each lane pairs up with its
+    // kInEpiWG epilogue warpgroups split the C channels of each half (a warp reaches only
+    // its own 32 TMEM lanes, so the split is by columns); each lane pairs up with its
     // neighbour token so that every store is one packed 4-byte pair (k, m..m+1)
     const int ew = (warp - 8) >> 2;
     const int wq = warp & 3;
@@ -251,7 +254,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const uint32_t acc = lane_addr + buf * 256;
 #pragma unroll 1
-        for (int c0 = ew * (C / 2); c0 < (ew + 1) * (C / 2); c0 += 16) {
+        for (int c0 = ew * (C / kInEpiWG); c0 < (ew + 1) * (C / kInEpiWG); c0 += 16) {
           uint32_t pg[32];  // P then G of 16 channels
           tmem_ld16x2_async(acc + c0, acc + C + c0, pg);
           tmem_wait_ld32(pg);
