@@ -504,9 +504,10 @@ def main():
     e2e_iters = max(3, min(args.steps, 5))
     e2e_serial_ms = timed(e2e_step, e2e_iters)
     e2e_ms, e2e_method = e2e_serial_ms, "serial: H2D, forward, D2H per call"
-    if world == 1:
+    if n % 8 == 0:
         # the host-tensor API: row slabs stream in and out on copy streams, and the copies of
-        # consecutive calls overlap (PCIe is full duplex)
+        # consecutive calls overlap (PCIe is full duplex); with P ranks each pipes its own
+        # rows and the bias rows are all-gathered between the two stages
         pipe = tops.triangle_attn.HostPipeline(pre, W_proj_g=inp["W_proj_g"], W_proj_o=inp["W_proj_o"],
                                                scale=scale)
         e2e_ms = timed(lambda: pipe(X_h, m_h, out_h), e2e_iters, finish=pipe.wait)

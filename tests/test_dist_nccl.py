@@ -88,3 +88,54 @@ def test_sharded_matches_single_gpu():
     for key in ("tri_attn", "outgoing", "incoming", "apb"):
         d = (res[key].float() - res["ref_" + key].float()).abs().max().item()
         assert d < 1e-2, f"{key}: sharded differs from single-GPU by {d}"
+
+
+def _pipe_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    import triangleops_b200 as tops
+    from triangleops_b200 import dist as tdist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        ta, _, _ = _inputs(dev)
+        N = ta["X"].shape[0]
+        r0, r1 = tdist.slab(N, rank, world)
+        mask = ta["mask"].clone()
+        for r in range(world):
+            mask[r * (N // world) + 3] = False  # a fully masked row in every rank's slab (same on all ranks)
+        pre = tops.triangle_attn.precompute(ta["W_ln"], ta["B_ln"], ta["WQ"], ta["WK"], ta["WV"], ta["Wz"], None, 4, 32)
+        pipe = tops.triangle_attn.HostPipeline(pre, W_proj_g=ta["Wg"], W_proj_o=ta["Wo"], scale=32**-0.5, slabs=4)
+        out = pipe(ta["X"][r0:r1].cpu().pin_memory(), mask[r0:r1].cpu().pin_memory())
+        pipe.wait()
+        torch.cuda.synchronize()
+        full = tdist.all_gather_rows(out.to(dev), 0).cpu()
+        if rank == 0:
+            ref = tops.triangle_attn.forward(ta["X"], pre, mask=mask, scale=32**-0.5, W_proj_g=ta["Wg"],
+                                             B_proj_g=None, W_proj_o=ta["Wo"], B_proj_o=None).cpu()
+            q.put((full, ref))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_pipeline_sharded_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_pipe_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full, ref = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    d = (full.float() - ref.float()).abs().max().item()
+    assert d < 1e-2, f"row-sharded host pipeline differs from single-GPU forward by {d}"

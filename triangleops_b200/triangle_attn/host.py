@@ -17,6 +17,10 @@ each buffer from being overwritten before its previous reader has finished. The
 work of a call is complete when ``wait(stream)`` returns on a stream (it makes that
 stream wait) or after ``torch.cuda.synchronize()``.
 
+With torch.distributed initialised (one process per GPU), each rank passes its own
+pair rows (rows [r*N/P, (r+1)*N/P) of X and the mask, and its rows of the output):
+the ranks' bias rows are all-gathered on the compute stream between the two stages.
+
 No counterpart in the reference (it takes device tensors only); the per-slab work is
 the same kernels as ``module.forward``.
 """
@@ -24,39 +28,42 @@ the same kernels as ``module.forward``.
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 
 from .. import _lib
 from .kernel import _mask_u8, gate_forward
 
 
 class HostPipeline:
-    def __init__(self, pre, *, W_proj_g, W_proj_o, scale=1.0, eps=1e-5, slabs=8):
+    def __init__(self, pre, *, W_proj_g, W_proj_o, scale=1.0, eps=1e-5, slabs=8, group=None):
         self.pre = pre
         self.Wg, self.Wo = W_proj_g, W_proj_o
         self.scale, self.eps, self.slabs = float(scale), float(eps), int(slabs)
+        self.group = group
         self._key = None
 
-    def _setup(self, N, C, dtype, dev):
+    def _setup(self, n, N, C, dtype, dev):
         H, D = self.pre["H"], self.pre["D"]
-        key = (N, C, H, D, dtype, dev)
+        key = (n, N, C, H, D, dtype, dev)
         if key == self._key:
             return
-        assert N % self.slabs == 0, f"N={N} must be divisible by slabs={self.slabs}"
+        assert n % self.slabs == 0, f"{n} rows must be divisible by slabs={self.slabs}"
         nkp = (N + 7) // 8 * 8
-        R = N // self.slabs
+        R = n // self.slabs
         f16 = torch.float16
-        self.N, self.C, self.R, self.nkp, self.H, self.D = N, C, R, nkp, H, D
-        self.x = torch.empty(N, N, C, dtype=dtype, device=dev)
-        self.m = torch.empty(N, N, dtype=torch.uint8, device=dev)
-        self.xln = torch.empty(N, N, C, dtype=dtype, device=dev)
-        self.q = torch.empty(N, H, N, D, dtype=f16, device=dev)
-        self.k = torch.empty(N, H, N, D, dtype=f16, device=dev)
-        self.vt = torch.empty(N, H, D, nkp, dtype=f16, device=dev)
-        self.maskf = torch.empty(N, nkp, dtype=f16, device=dev)
+        self.n, self.N, self.C, self.R, self.nkp, self.H, self.D = n, N, C, R, nkp, H, D
+        self.x = torch.empty(n, N, C, dtype=dtype, device=dev)
+        self.m = torch.empty(n, N, dtype=torch.uint8, device=dev)
+        self.xln = torch.empty(n, N, C, dtype=dtype, device=dev)
+        self.q = torch.empty(n, H, N, D, dtype=f16, device=dev)
+        self.k = torch.empty(n, H, N, D, dtype=f16, device=dev)
+        self.vt = torch.empty(n, H, D, nkp, dtype=f16, device=dev)
+        self.maskf = torch.empty(n, nkp, dtype=f16, device=dev)
         self.bias_slab = torch.empty(self.slabs, H, R, nkp, dtype=f16, device=dev)
+        self.bias_local = torch.empty(H, n, nkp, dtype=f16, device=dev)
         self.bias = torch.empty(H, N, nkp, dtype=f16, device=dev)
-        self.o = torch.empty(N, N, H * D, dtype=dtype, device=dev)
-        self.out = torch.empty(N, N, C, dtype=dtype, device=dev)
+        self.o = torch.empty(n, N, H * D, dtype=dtype, device=dev)
+        self.out = torch.empty(n, N, C, dtype=dtype, device=dev)
         self.w = self.pre["W_qkvz"] if self.pre["W_qkvz"].dtype == dtype else self.pre["W_qkvz"].to(dtype)
         self.h2d = torch.cuda.Stream(dev)
         self.d2h = torch.cuda.Stream(dev)
@@ -66,21 +73,25 @@ class HostPipeline:
         self._key = key
 
     def __call__(self, X_host, mask_host=None, out_host=None):
-        """Enqueue one forward of X_host (N, N, C) pinned; the result lands in out_host
-        (allocated pinned if None, returned). mask_host: (N, N) bool/int, pinned, or None."""
-        N, _, C = X_host.shape
+        """Enqueue one forward of X_host (n, N, C) pinned — the whole (N, N, C) pair tensor,
+        or this rank's n = N/P pair rows when torch.distributed is initialised; the result
+        lands in out_host (allocated pinned if None, returned). mask_host: the same rows of
+        the (N, N) bool/int mask, pinned, or None."""
+        n, N, C = X_host.shape
+        world = dist.get_world_size(self.group) if dist.is_available() and dist.is_initialized() else 1
+        assert n * world == N, f"X_host holds {n} rows of {N}: expected N / world = {N // world}"
         dev = torch.device("cuda", torch.cuda.current_device())
         _lib.require_cuda(torch.empty(0, device=dev))
-        self._setup(N, C, X_host.dtype, dev)
+        self._setup(n, N, C, X_host.dtype, dev)
         if out_host is None:
-            out_host = torch.empty(N, N, C, dtype=X_host.dtype).pin_memory()
+            out_host = torch.empty(n, N, C, dtype=X_host.dtype).pin_memory()
         dead = None
         if mask_host is not None:
-            mask_host = mask_host.reshape(N, N)
+            mask_host = mask_host.reshape(n, N)
             if mask_host.dtype == torch.bool:
                 mask_host = mask_host.view(torch.uint8)  # same bytes, still pinned
             elif mask_host.dtype != torch.uint8:
-                mask_host = _mask_u8(mask_host, (N, N))
+                mask_host = _mask_u8(mask_host, (n, N))
             # fully masked rows (the reference's -1e9 turns them into a uniform average
             # over all keys; the kernel drops masked keys): found on the host, no sync
             dead = (~mask_host.bool().any(dim=1)).nonzero().flatten()
@@ -106,8 +117,14 @@ class HostPipeline:
                       self.xln[r0].data_ptr(), self.q[r0].data_ptr(), self.k[r0].data_ptr(), self.vt[r0].data_ptr(),
                       self.maskf[r0].data_ptr(), self.bias_slab[i].data_ptr(), st)
             self.ev_proj[i].record(compute)
-        # the shared bias, [H][N][Np], from the slabs' [H][R][Np] blocks
-        self.bias.view(H, self.slabs, R, nkp).copy_(self.bias_slab.permute(1, 0, 2, 3))
+        # the shared bias, [H][N][Np], from the slabs' [H][R][Np] blocks (and the other ranks' rows)
+        if world == 1:
+            self.bias.view(H, self.slabs, R, nkp).copy_(self.bias_slab.permute(1, 0, 2, 3))
+        else:
+            self.bias_local.view(H, self.slabs, R, nkp).copy_(self.bias_slab.permute(1, 0, 2, 3))
+            gathered = torch.empty(world, H, n, nkp, dtype=self.bias.dtype, device=dev)
+            dist.all_gather_into_tensor(gathered.view(-1), self.bias_local.view(-1), group=self.group)
+            self.bias.view(H, world, n, nkp).copy_(gathered.permute(1, 0, 2, 3))
         # --- stage B: attention + gate per slab, each slab out while the next computes
         for i in range(self.slabs):
             r0, r1 = i * R, (i + 1) * R
