@@ -1,9 +1,9 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container that has a checkout of youngchan2/TriangleOps (default
-``/root/reference``; override with ``TRIANGLEOPS_REF``)::
+Run where a checkout of youngchan2/TriangleOps is available, its path in
+``TRIANGLEOPS_REF``::
 
-    python tests/golden/make_golden.py
+    TRIANGLEOPS_REF=<path to the checkout> python tests/golden/make_golden.py
 
 It imports the reference's own pure-torch functions
 (``benchmarks/references.py``: ``torch_triangle_attention`` :174-205,
@@ -21,7 +21,7 @@ import sys
 
 import torch
 
-REF = os.environ.get("TRIANGLEOPS_REF", "/root/reference")
+REF = os.environ.get("TRIANGLEOPS_REF", "")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.pt")
 
 
@@ -33,6 +33,8 @@ def _load(name, path):
 
 
 def main():
+    if not REF or not os.path.isdir(REF):
+        sys.exit("set TRIANGLEOPS_REF to a checkout of youngchan2/TriangleOps")
     refs = _load("ref_references", os.path.join(REF, "benchmarks", "references.py"))
     lnabs = _load("ref_ln_absorption", os.path.join(REF, "triangle_ops", "_common", "ln_absorption.py"))
     g = torch.Generator().manual_seed(1234)
