@@ -234,3 +234,72 @@ def test_sharded_attention_pair_bias_gloo():
                                             w["Wg"], w["Wo"], H, D, key_mask=km, scale=0.5, B_proj_g=w["Bg"],
                                             B_proj_o=w["Bo"])
     assert (full - ref).abs().max().item() < 1e-4
+
+
+def _chain_inputs():
+    g = torch.Generator().manual_seed(21)
+    N, C, H, D = 8, 16, 2, 8
+    r = lambda *s, sd=1.0: torch.randn(*s, generator=g) * sd  # noqa: E731
+
+    def tm():
+        return dict(norm_in_weight=1 + 0.1 * r(C), norm_in_bias=0.1 * r(C), p_in_weight=r(2 * C, C, sd=C**-0.5),
+                    g_in_weight=r(2 * C, C, sd=C**-0.5), norm_out_weight=1 + 0.1 * r(C), norm_out_bias=0.1 * r(C),
+                    p_out_weight=r(C, C, sd=C**-0.5), g_out_weight=r(C, C, sd=C**-0.5))
+
+    def ta():
+        return dict(W_ln=1 + 0.1 * r(C), B_ln=0.1 * r(C), WQ=r(C, H * D, sd=C**-0.5), WK=r(C, H * D, sd=C**-0.5),
+                    WV=r(C, H * D, sd=C**-0.5), W_proj_z=r(C, H, sd=C**-0.5), B_proj_z=0.1 * r(H),
+                    W_proj_g=r(C, C, sd=C**-0.5), W_proj_o=r(C, C, sd=C**-0.5), H=H, D=D)
+
+    w = dict(tri_mul_out=tm(), tri_mul_in=tm(), tri_attn_start=ta(), tri_attn_end=ta())
+    mask = torch.rand(N, N, generator=g) > 0.2
+    return r(N, N, C), w, mask
+
+
+def _chain_pre(w):
+    pre = {k: {"w": w[k]} for k in ("tri_mul_out", "tri_mul_in")}
+    for k in ("tri_attn_start", "tri_attn_end"):
+        a = w[k]
+        pre[k] = dict(H=a["H"], D=a["D"], W_ln=a["W_ln"], B_ln=a["B_ln"], WQ=a["WQ"], WK=a["WK"], WV=a["WV"],
+                      Wz=a["W_proj_z"], BZ=a["B_proj_z"], W_qkvz=torch.cat([a["WQ"].t(), a["WK"].t(), a["WV"].t()]),
+                      W_proj_g=a["W_proj_g"], W_proj_o=a["W_proj_o"])
+    return pre
+
+
+def _chain_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, w, mask = _chain_inputs()
+        N = x.shape[0]
+        r0, r1 = tdist.slab(N, rank, world)
+        out = tdist.pair_update_rows(x[r0:r1].contiguous(), _chain_pre(w), mask=mask, attn_ops=CpuOps,
+                                     trimul_ops=CpuTrimulOps)
+        full = tdist.all_gather_rows(out.contiguous(), 0)
+        if rank == 0:
+            q.put(full)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_transpose_rows_single_rank():
+    x = torch.arange(4 * 4 * 3, dtype=torch.float32).reshape(4, 4, 3)
+    assert torch.equal(tdist.transpose_rows(x), x.transpose(0, 1))
+
+
+def test_sharded_pairformer_chain_gloo():
+    """Row-sharded chain (all-to-all transposes for the incoming multiplication and the
+    ending node) on 2 gloo ranks with CPU stand-ins equals the unsharded oracle chain."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_chain_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    full = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, w, mask = _chain_inputs()
+    ref = oracle.pair_update(x, mask=mask, **w)
+    assert (full - ref).abs().max().item() < 1e-4

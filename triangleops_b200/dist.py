@@ -22,6 +22,9 @@ only where the algorithm exchanges data:
   projects K and V for every key itself. No collective: the M*2*H*D K/V elements
   are cheaper to recompute than to exchange.
 
+* the Pairformer chain (``pair_update_rows``): row-sharded x, with all-to-all
+  transposes where a step needs columns (incoming multiplication, ending node).
+
 The per-rank compute steps are looked up on an ``ops`` object so that the host
 logic (slab partitioning, collective assembly) is testable with gloo on CPU.
 """
@@ -114,22 +117,19 @@ class TrimulKernelOps:
         return output_phase_tokens(y, x_tokens, pre, eps)
 
 
-def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-5, group=None, ops=TrimulKernelOps):
-    """Rows [r0, r1) of the triangle multiplicative update of the replicated pair tensor
-    x (1, L, L, C); returns (1, n, L, C). Collective: all-gather of this rank's b."""
-    if direction not in ("outgoing", "incoming"):
-        raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
-    B, L, _, C = x.shape
-    assert B == 1, "row-slab sharding takes one pair tensor"
+def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
+    """The triangle multiplicative update of this rank's pair rows from its row slab
+    x_rows (n, L, C) = x[r0:r1] and, for the incoming direction, its column slab given
+    as rows of x^T, x_colsT (n, L, C) = x[:, r0:r1]^T. mask: the full (L, L) mask or None."""
+    n, L, C = x_rows.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     r0, r1 = slab(L, rank, world)
-    n = r1 - r0
     if direction == "outgoing":  # a rows i in slab, b rows j in slab: tokens (i, k)
-        xs = x[0, r0:r1].reshape(n * L, C)
+        xs = x_rows.reshape(n * L, C)
         ms = None if mask is None else mask.reshape(L, L)[r0:r1].reshape(n * L)
     else:  # a columns i in slab, b columns j in slab: tokens (k, i)
-        xs = x[0, :, r0:r1].contiguous().reshape(L * n, C)
+        xs = x_colsT.transpose(0, 1).contiguous().reshape(L * n, C)
         ms = None if mask is None else mask.reshape(L, L)[:, r0:r1].contiguous().reshape(L * n)
     ab = ops.input_phase(xs.contiguous(), ms, pre, eps)  # (2C, n*L) as [d][i][k] or [d][k][i]
     a = ab[:C].reshape(C, n, L) if direction == "outgoing" else ab[:C].reshape(C, L, n)
@@ -141,8 +141,63 @@ def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-
     else:
         b_chunks = b.unsqueeze(0)
     y = ops.contract_slab(a, b_chunks, direction, n, L, world)  # (C, n, L)
-    out = ops.output_phase(y.reshape(C, n * L), x[0, r0:r1].reshape(n * L, C).contiguous(), pre, eps)
-    return out.reshape(1, n, L, C)
+    out = ops.output_phase(y.reshape(C, n * L), x_rows.reshape(n * L, C).contiguous(), pre, eps)
+    return out.reshape(n, L, C)
+
+
+def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-5, group=None, ops=TrimulKernelOps):
+    """Rows [r0, r1) of the triangle multiplicative update of the replicated pair tensor
+    x (1, L, L, C); returns (1, n, L, C). Collective: all-gather of this rank's b."""
+    if direction not in ("outgoing", "incoming"):
+        raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
+    B, L, _, C = x.shape
+    assert B == 1, "row-slab sharding takes one pair tensor"
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    r0, r1 = slab(L, rank, world)
+    x_colsT = None if direction == "outgoing" else x[0, :, r0:r1].transpose(0, 1)
+    return _trimul_from_slabs(x[0, r0:r1], x_colsT, pre, direction, mask, eps, group, ops).unsqueeze(0)
+
+
+def transpose_rows(x_rows, group=None):
+    """Rows [r0, r1) of x (n, N, C) -> the same rows of x^T, i.e. x[:, r0:r1]^T (n, N, C),
+    by one all-to-all: rank r sends its (n, n, C) block of columns [j0, j1) to rank j."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    n, N, C = x_rows.shape
+    if world == 1:
+        return x_rows.transpose(0, 1).contiguous()
+    assert n * world == N
+    send = x_rows.reshape(n, world, n, C).permute(1, 0, 2, 3).contiguous()  # [dest][i][k][C]
+    recv = torch.empty_like(send)  # [src][i of src's rows][k of my columns][C]
+    dist.all_to_all_single(recv.view(-1), send.view(-1), group=group)
+    return recv.permute(2, 0, 1, 3).reshape(n, N, C)  # x^T[k][src * n + i]
+
+
+def pair_update_rows(x_rows, pre, *, mask=None, scale=None, eps=1e-5, group=None, attn_ops=KernelOps,
+                     trimul_ops=TrimulKernelOps):
+    """The Pairformer pair-update chain (``pairformer.pair_update``) on a row-sharded pair
+    tensor: x_rows (n, N, C) holds rows [r0, r1) of x, mask is the full (N, N) mask (or
+    None) on every rank; returns the updated rows. Collectives: the b all-gathers of the
+    two triangle multiplications, the shared-bias all-gathers of the two attentions, and
+    three all-to-all transposes (x^T for the incoming multiplication and the ending-node
+    attention, and the ending node's result back to rows)."""
+    n, N, _ = x_rows.shape
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    r0, r1 = slab(N, rank, world)
+    m = None if mask is None else mask.reshape(N, N)
+    x_rows = x_rows + _trimul_from_slabs(x_rows, None, pre["tri_mul_out"], "outgoing", m, eps, group, trimul_ops)
+    x_rows = x_rows + _trimul_from_slabs(x_rows, transpose_rows(x_rows, group), pre["tri_mul_in"], "incoming", m, eps,
+                                         group, trimul_ops)
+    for name, ending in (("tri_attn_start", False), ("tri_attn_end", True)):
+        p = pre[name]
+        sc = p["D"] ** -0.5 if scale is None else scale
+        src = transpose_rows(x_rows, group) if ending else x_rows
+        mr = None if m is None else (m.t() if ending else m)[r0:r1].contiguous()
+        o = triangle_attention_rows(src.contiguous(), p, N=N, mask_rows=mr, scale=sc, eps=eps,
+                                    W_proj_g=p["W_proj_g"], W_proj_o=p["W_proj_o"], group=group, ops=attn_ops)
+        x_rows = x_rows + (transpose_rows(o, group) if ending else o)
+    return x_rows
 
 
 class ApbKernelOps:
