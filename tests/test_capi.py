@@ -105,3 +105,39 @@ def test_workspace_bytes_match_the_python_layer():
     assert list(out)[:5] == [H * M * D * 2, H * M * D * 2, H * D * mp * 2, mp * 2, H * Mq * mp * 4]
     assert lib.tops_apb_workspace_bytes(I64(M), I64(M + 1), I64(H), I64(D), out) == _lib.ERR_SHAPE
     assert lib.tops_apb_workspace_bytes(I64(M), I64(M), I64(H), I64(D), None) == _lib.ERR_ARG
+
+
+def test_extension_entry_points_validate_on_the_host():
+    """The entry points without a reference counterpart reject bad arguments before any
+    device work (so these run without a GPU)."""
+    lib = ctypes.CDLL(_build.build())
+    P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    f = lib.tops_apb_forward_rows
+    f.argtypes = [I, I64, I64, I64, I64, I64, I64, I64] + [P] * 7 + [F, F] + [P] * 7
+    base = [P(16)] * 7
+    ws = [P(16)] * 7
+    assert f(_lib.BF16, 256, 200, 100, 128, 128, 4, 32, *base, 1.0, 1e-5, *ws) == _lib.ERR_SHAPE  # q0 + Mq > M
+    assert f(2, 256, 0, 256, 128, 128, 4, 32, *base, 1.0, 1e-5, *ws) == _lib.ERR_DTYPE
+    g = lib.tops_trimul_input_phase
+    g.argtypes = [I, I64, I64, P, P, P, P, P, F, P, P]
+    assert g(_lib.BF16, 10, 128, 16, None, 16, 16, 16, 1e-5, 16, None) == _lib.ERR_ALIGN  # M % 8 != 0
+    h = lib.tops_triangle_attn_project_transposed
+    h.argtypes = [I, I64, I64, I64, I64, I64, P, I, P, P, P, P, P, F, F] + [P] * 7
+    assert h(_lib.BF16, 10, 130, 128, 4, 32, 16, 1, 16, 16, 16, 16, None, 1.0, 1e-5, *([P(16)] * 6), None) == \
+        _lib.ERR_ALIGN  # column stride N*C*2 must be a multiple of 16
+    k = lib.tops_fused_gate_residual
+    k.argtypes = [I, I64, I64, P, P, P, P, P, P, P, P, I64, P]
+    assert k(_lib.BF16, 100, 128, 16, 16, 16, 16, None, None, 16, 16, 7, None) == _lib.ERR_SHAPE  # T % trans_n
+    o = lib.tops_trimul_output_phase_residual
+    o.argtypes = [I, I64, I64, P, P, P, P, P, F, P, P, P]
+    assert o(_lib.BF16, 64, 128, 16, 16, 16, 16, 16, 1e-5, None, 16, None) == _lib.ERR_ALIGN  # no residual
+
+
+def test_pairformer_shape_checks_on_host():
+    import torch
+    import triangleops_b200 as tops
+
+    with pytest.raises(AssertionError):
+        tops.pairformer.pair_update(torch.zeros(10, 10, 128), {}, mask=None)  # N % 8
+    with pytest.raises(AssertionError):
+        tops.pairformer.pair_update(torch.zeros(8, 8, 128), {}, stages=("tri_mul_sideways",))
