@@ -47,22 +47,35 @@ __global__ void __launch_bounds__(256) zbias_kernel(const T* __restrict__ z, ZBi
   }
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const long long wid = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  // the next group's 32 bytes per lane are loaded before this group is reduced, so two
+  // groups' loads are in flight per warp (the kernel is bound by loads in flight; a
+  // third group measured no faster)
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  auto load = [&](long long t, uint4& u0, uint4& u1) {
+    if (t < a.n_tok) {
+      const uint4* src = reinterpret_cast<const uint4*>(z + t * CZ);
+      u0 = __ldcs(src + sub);
+      u1 = __ldcs(src + 8 + sub);
+    } else {
+      u0 = zero;
+      u1 = zero;
+    }
+  };
+  uint4 nx0, nx1;
+  load(wid * 4 + grp, nx0, nx1);
   for (long long base = wid * 4; base < a.n_tok; base += warps * 4) {
     const long long tok = base + grp;
     const bool valid = tok < a.n_tok;
+    const uint4 u0 = nx0, u1 = nx1;
+    load(base + warps * 4 + grp, nx0, nx1);
     float v[16];
-    if (valid) {
-      const uint4* src = reinterpret_cast<const uint4*>(z + tok * CZ);
-      const uint4 u0 = __ldcs(src + sub), u1 = __ldcs(src + 8 + sub);
+    {
       const uint32_t p[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         v[2 * e] = E::lo(p[e]);
         v[2 * e + 1] = E::hi(p[e]);
       }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 16; ++e) v[e] = 0.f;
     }
     float mean = 0.f;
 #pragma unroll
