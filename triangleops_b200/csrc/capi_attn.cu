@@ -176,7 +176,7 @@ int launch_gate(int dtype, int64_t T_, const void* o, const void* gin, const voi
   set_smem(kern, smem);
   const int tiles = static_cast<int>((T_ + 127) / 128);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, 384, smem, st>>>(mg, mo, mwg, mwo, args);
+  kern<<<grid, 640, smem, st>>>(mg, mo, mwg, mwo, args);
   return launch_status();
 }
 

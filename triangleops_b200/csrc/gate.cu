@@ -10,8 +10,9 @@
 // rounds to the IO dtype — the rounding point of the reference — and writes the
 // product over the gin tile (gin is dead once MMA1 completes); MMA2 acc2 = that
 // product times Wo^T; the warpgroup adds bo (and optionally a residual: the
-// Pairformer update x += op(x), in place) and stores, optionally transposed. Two warpgroups alternate
-// tiles, each with its own TMEM accumulator pair, and MMA1 of the next tile is
+// Pairformer update x += op(x), in place) and stores, optionally transposed. Two pairs of warpgroups
+// alternate tiles, each pair with its own TMEM accumulator pair and each warpgroup of
+// a pair taking half of the C channels, and MMA1 of the next tile is
 // issued before MMA2 of the current one so the tensor core never waits on a gate.
 #include "sm100.cuh"
 
@@ -48,7 +49,7 @@ struct GateArgs {
 };
 
 template <typename T, int C>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(640, 1)
     gate_kernel(const __grid_constant__ CUtensorMap map_gin, const __grid_constant__ CUtensorMap map_o,
                 const __grid_constant__ CUtensorMap map_wg, const __grid_constant__ CUtensorMap map_wo, GateArgs a) {
   using Cfg = GateCfg<C>;
@@ -64,9 +65,9 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&sm.in_full[s], 1);
       mbar_init(&sm.in_empty[s], 1);
       mbar_init(&sm.acc1_full[s], 1);
-      mbar_init(&sm.a2_ready[s], 4);
+      mbar_init(&sm.a2_ready[s], 8);
       mbar_init(&sm.acc2_full[s], 1);
-      mbar_init(&sm.acc_free[s], 4);
+      mbar_init(&sm.acc_free[s], 8);
     }
     sm.abort = 0;
     fence_mbar_init();
@@ -134,8 +135,9 @@ __global__ void __launch_bounds__(384, 1)
       }
     }
   } else if (warp >= 4) {
-    const int wg = (warp - 4) >> 2;
+    const int wg = (warp - 4) >> 3;           // tile slot (alternate tiles)
     const int wq = warp & 3;
+    const int half = ((warp - 4) >> 2) & 1;  // column half of the slot's tile
     const int row = wq * 32 + lane;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     int it = wg;
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(384, 1)
       uint8_t* gtile = sm.gin[s];
       const uint8_t* otile = sm.o[s];
 #pragma unroll 1
-      for (int c0 = 0; c0 < C; c0 += 32) {
+      for (int c0 = half * (C / 2); c0 < (half + 1) * (C / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(acc1 + c0, r);
 #pragma unroll
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(384, 1)
       T* dst = static_cast<T*>(a.out) + orow * C;
       const T* res = a.residual != nullptr ? static_cast<const T*>(a.residual) + orow * C : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < C; c0 += 32) {
+      for (int c0 = half * (C / 2); c0 < (half + 1) * (C / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32(acc2 + c0, r);
         if (tok < a.T) {
