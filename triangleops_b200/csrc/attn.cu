@@ -36,9 +36,12 @@
 //
 // Online softmax in the exp2 domain (Q carries scale*log2(e) and the bias log2(e),
 // both folded in upstream) with lazy rescaling (O is only rescaled when the running
-// max grows by more than 2^8). The per-element work runs on f16 pairs: S + bias is
-// rounded to f16 (relative error 2^-11, well below the 2^-8 rounding the 16-bit Q
-// and K already put into S), the row max is a pairwise tree, and
+// max grows by more than 2^8). The per-element work runs on f16 pairs: with the f16
+// bias the tensor core accumulates S = bias x I + Q K^T in f16 (the bias terms are
+// exact, each of the D/16 Q K^T steps rounds once, relative error 2^-11 each, below
+// the 2^-8 rounding the 16-bit Q and K already put into S) and the softmax loads it
+// as packed pairs (tcgen05.ld .pack::16b: no conversion); the fp32 bias path rounds
+// S + bias to f16 pairs itself. The row max is a pairwise tree, and
 // P = 2^(x - m), 2/3 of the pairs on the MUFU (ex2.approx.f16x2, which issues twice
 // on the XU pipe) and 1/3 by a polynomial on the FMA pipe (ex2_poly_f16x2), so that
 // neither pipe alone bounds the step; V^T and the mask row are f16 for the PV MMA.
@@ -52,6 +55,9 @@ namespace tops {
 constexpr bool kPolyExp = TOPS_POLY_EXP != 0;
 #ifndef TOPS_POLY_PICK
 #define TOPS_POLY_PICK(c) ((c) % 3 == 1)  // pairs whose 2^x takes the polynomial (11 of 32)
+#endif
+#ifndef TOPS_S_F16
+#define TOPS_S_F16 1  // f16 bias path: S accumulated in f16 by the tensor core, loaded packed
 #endif
 #ifndef TOPS_ATTN_SMEM_KB
 #define TOPS_ATTN_SMEM_KB 200  // operand budget (Q tiles + stages); the B200 allows 227 KB per CTA
@@ -272,7 +278,9 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, TQ, BF32>::THREADS, 1)
     if (lane == 0) {
       // ---------------- QK^T issuer of tile t ----------------
       const int t = warp - 1;
-      const uint32_t idesc_qk = make_idesc_f16(128, BK, 0, false, false);  // Q, K are f16
+      // Q, K are f16; S is fp32, or f16 (D format 0) for the f16-bias path with TOPS_S_F16
+      const uint32_t idesc_qk =
+          make_idesc_f16(128, BK, 0, false, false) & ((!BF32 && TOPS_S_F16) ? ~(3u << 4) : ~0u);
       const uint32_t qa = smem_u32(sm.q[t]);
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       bool ok = true;
@@ -390,6 +398,8 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, TQ, BF32>::THREADS, 1)
                   __floats2half2_rn(__uint_as_float(sv[ch * 4 + 2]) + bf.z, __uint_as_float(sv[ch * 4 + 3]) + bf.w);
             }
           }
+        } else if (TOPS_S_F16) {
+          tmem_ld64_pack16(lane_addr + Cfg::S_COL + t * 64, reinterpret_cast<uint32_t*>(xh));
         } else {
           uint32_t sv[64];
           tmem_ld64(lane_addr + Cfg::S_COL + t * 64, sv);
