@@ -9,15 +9,24 @@ namespace tops {
 
 template <typename T, int C>
 int launch_trimul_in(int dtype, const void* x, const void* w, const LnGateArgs& args, cudaStream_t st) {
-  CUtensorMap mx, mw;
+  CUtensorMap mx, mw, mo;
   if (!map_rows(&mx, dtype, x, args.M, C, 128)) return TOPS_ERR_TMAP;
   if (!map_rows(&mw, dtype, w, 4 * C, C, C)) return TOPS_ERR_TMAP;  // C-row boxes, placed by half
+  {
+    // ab, D-major [2C][M]: boxes of 32 tokens x 8 channels, one per epilogue warp and step
+    const uint64_t dims[2] = {static_cast<uint64_t>(args.M), static_cast<uint64_t>(2 * C)};
+    const uint64_t str[1] = {static_cast<uint64_t>(args.M) * 2};
+    const uint32_t box[2] = {32, 8};
+    if (!make_tmap(&mo, tmap_dtype(dtype), 2, args.out, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return TOPS_ERR_TMAP;
+  }
   const size_t smem = sizeof(TmInSmem<C>) + 1024;
+  static_assert(sizeof(TmInSmem<C>) + 1024 <= 227 * 1024, "input phase shared memory");
   auto kern = trimul_in_kernel<T, C>;
   set_smem(kern, smem);
   const long long tiles = (args.M + 127) / 128;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 256 + 128 * kInEpiWG, smem, st>>>(mx, mw, args);
+  kern<<<grid, 256 + 128 * kInEpiWG, smem, st>>>(mx, mw, mo, args);
   return launch_status();
 }
 

@@ -16,6 +16,10 @@
 
 namespace tops {
 
+#ifndef TOPS_L2_PREFETCH
+#define TOPS_L2_PREFETCH 4  // tiles ahead that the streaming phases prefetch into L2 (0: off)
+#endif
+
 struct LnGateArgs {
   long long M;           // tokens
   float eps;
@@ -27,64 +31,124 @@ struct LnGateArgs {
 };
 
 // LayerNorm statistics of a 128 x C row-major (K-major, SW128) staged tile row
-// (two passes over shared memory, 16-byte chunks: no C-wide register array).
+// (two passes over shared memory, 16-byte chunks: no C-wide register array; four
+// packed fp32-pair accumulators, so the adds form eight independent chains).
 template <typename T, int C>
 __device__ __forceinline__ void row_stats_kmajor(const uint8_t* tile, int row, float& mean, float& rstd, float eps) {
   using E = Elem<T>;
   auto chunk = [&](int i) {  // chunk i of the row: channels [8i, 8i + 8)
     return *reinterpret_cast<const uint4*>(tile + (i >> 3) * 16384 + sw128_off(row, i & 7));
   };
-  float s = 0.f;
+  unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll 4
   for (int i = 0; i < C / 8; ++i) {
     const uint4 u = chunk(i);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) s += E::lo(w[e]) + E::hi(w[e]);
+    for (int e = 0; e < 4; ++e) acc[e] = f2_add(acc[e], f2_pack(E::lo(w[e]), E::hi(w[e])));
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float lo, hi;
+    f2_unpack(acc[e], lo, hi);
+    s += lo + hi;
+    acc[e] = 0ull;
   }
   mean = s * (1.0f / C);
-  float v = 0.f;
+  const unsigned long long nm = f2_pack(-mean, -mean);
 #pragma unroll 4
   for (int i = 0; i < C / 8; ++i) {
     const uint4 u = chunk(i);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float d0 = E::lo(w[e]) - mean, d1 = E::hi(w[e]) - mean;
-      v = fmaf(d0, d0, fmaf(d1, d1, v));
+      const unsigned long long d = f2_add(f2_pack(E::lo(w[e]), E::hi(w[e])), nm);
+      acc[e] = f2_fma(d, d, acc[e]);
     }
+  }
+  float v = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float lo, hi;
+    f2_unpack(acc[e], lo, hi);
+    v += lo + hi;
   }
   rstd = rsqrtf(v * (1.0f / C) + eps);
 }
 
-// LayerNorm statistics over the K (= channel) axis of token `tok` of a C x 128
-// MN-major SW128 staged tile (two 64-token halves, each C rows of 128 B).
+// LayerNorm statistics over the channel (K) axis of the 128 tokens of a C x 128
+// MN-major SW128 staged tile (two 64-token halves, each C rows of 128 B), computed by
+// one warpgroup together (wtid = thread index within it). Thread (warp w, lane) takes
+// token group tg = 4w + lane/8 (tokens 8tg..8tg+7, one 16-byte chunk per channel) and
+// channel subset cs = lane%8 (C/8 channels); the 8 lanes of a group combine their
+// partial sums with a butterfly reduce-scatter, so lane cs ends with token 8tg + cs.
+// Two passes (mean, then squared deviations). Returns the token (within the tile)
+// whose statistics this thread holds; its 32 tokens are the warp's own 32 rows.
 template <typename T, int C>
-__device__ __forceinline__ void col_stats_mnmajor(const uint8_t* tile, int tok, float& mean, float& rstd, float eps) {
+__device__ __forceinline__ int col_stats_coop(const uint8_t* tile, int wtid, float& mean, float& rstd, float eps) {
   using E = Elem<T>;
-  const uint8_t* base = tile + (tok >> 6) * (C * 128) + (tok & 7) * 2;
-  const uint32_t chunk = (tok & 63) >> 3;
-  // two passes over shared memory (mean, then squared deviations): no C-float register array
-  auto val = [&](int d) {
-    const uint16_t u = *reinterpret_cast<const uint16_t*>(base + d * 128 + ((chunk ^ (d & 7)) << 4));
-    return E::lo(static_cast<uint32_t>(u));
+  constexpr int CS = C / 8;  // channels per subset
+  static_assert((CS & (CS - 1)) == 0 && CS >= 8, "C / 8 must be a power of two >= 8");
+  const int lane = wtid & 31, cs = lane & 7, tg = (wtid >> 5) * 4 + (lane >> 3);
+  const uint8_t* base = tile + (tg >> 3) * (C * 128);
+  const uint32_t chunk = tg & 7;
+  auto ld = [&](int i) {
+    // channel order rotated by cs: the 8 lanes of a group read 8 different 16-byte bank groups
+    const int d = cs * CS + ((i + cs) & (CS - 1));
+    return *reinterpret_cast<const uint4*>(base + d * 128 + ((chunk ^ (d & 7)) << 4));
   };
-  float s = 0.f;
-#pragma unroll 16
-  for (int d = 0; d < C; ++d) s += val(d);
-  mean = s * (1.0f / C);
-  float v = 0.f;
-#pragma unroll 16
-  for (int d = 0; d < C; ++d) {
-    const float dd = val(d) - mean;
-    v = fmaf(dd, dd, v);
+  auto reduce8 = [&](const unsigned long long (&acc)[4]) -> float {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f2_unpack(acc[e], v[2 * e], v[2 * e + 1]);
+    const bool b2 = cs & 4, b1 = cs & 2, b0 = cs & 1;
+    float t[4], u[2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = (b2 ? v[4 + j] : v[j]) + __shfl_xor_sync(0xffffffffu, b2 ? v[j] : v[4 + j], 4);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) u[j] = (b1 ? t[2 + j] : t[j]) + __shfl_xor_sync(0xffffffffu, b1 ? t[j] : t[2 + j], 2);
+    return (b0 ? u[1] : u[0]) + __shfl_xor_sync(0xffffffffu, b0 ? u[0] : u[1], 1);
+  };
+  unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll 4
+  for (int i = 0; i < CS; ++i) {
+    const uint4 u = ld(i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] = f2_add(acc[e], f2_pack(E::lo(w[e]), E::hi(w[e])));
   }
-  rstd = rsqrtf(v * (1.0f / C) + eps);
+  mean = reduce8(acc) * (1.0f / C);
+  unsigned long long nm[4];
+  const int g0 = lane & ~7;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    nm[e] = f2_pack(-__shfl_sync(0xffffffffu, mean, g0 + 2 * e), -__shfl_sync(0xffffffffu, mean, g0 + 2 * e + 1));
+    acc[e] = 0ull;
+  }
+#pragma unroll 4
+  for (int i = 0; i < CS; ++i) {
+    const uint4 u = ld(i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const unsigned long long d = f2_add(f2_pack(E::lo(w[e]), E::hi(w[e])), nm[e]);
+      acc[e] = f2_fma(d, d, acc[e]);
+    }
+  }
+  rstd = rsqrtf(reduce8(acc) * (1.0f / C) + eps);
+  return tg * 8 + cs;
 }
 
 // ===========================================================================
 // input phase
 // ===========================================================================
+// epilogue warpgroups of the input phase (each takes C / kInEpiWG channels of a half)
+#ifndef TOPS_IN_EPI_WG
+#define TOPS_IN_EPI_WG 4
+#endif
+constexpr int kInEpiWG = TOPS_IN_EPI_WG;
+
 template <int C>
 struct TmInSmem {
   static constexpr int NOUT = 4 * C;
@@ -92,25 +156,45 @@ struct TmInSmem {
   // weights per 64-channel K atom, rows reordered by halves: [P(0:C) G(0:C) P(C:2C) G(C:2C)]
   alignas(1024) uint8_t w[(C / 64) * NOUT * 128];
   alignas(1024) uint8_t x[2][TILE];
-  float mean[2][128];
+  // the LayerNorm terms as one more K step of 16 (K-major, 32-byte swizzle): per token
+  // [-mean hi, -mean lo, -mean hi, 1/rstd hi, 1/rstd lo, 1/rstd hi, 0...] against, per
+  // output channel, [sumW hi, sumW hi, sumW lo, Bc hi, Bc hi, Bc lo, 0...]
+  alignas(1024) uint8_t aext[2][128 * 32];
+  alignas(1024) uint8_t bext[2][2 * C * 32];
+  // per epilogue warp: 8 channels x 32 tokens of the D-major output, stored by TMA
+  alignas(128) uint8_t stage[4 * kInEpiWG][8 * 32 * 2];
   float rstd[2][128];
-  alignas(16) float sum_w[NOUT];     // folded LN constants; the G halves pre-scaled by 1/2 (tanh form)
-  alignas(16) float b_const[NOUT];
-  uint64_t bar_w, x_full[2], x_empty[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
+  uint64_t bar_w, x_full[2], x_empty[2], ext_full[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
 };
 
-// epilogue warpgroups of the input phase (each takes C / kInEpiWG channels of a half)
-constexpr int kInEpiWG = 4;
+// element k (< 8) of row r of a K-major 32-byte-swizzled tile of 16-bit values: byte offset
+__device__ __forceinline__ uint32_t sw32_chunk_off(uint32_t r, uint32_t chunk) {
+  return r * 32u + ((chunk ^ ((r >> 2) & 1u)) << 4);
+}
+
+// v = hi + lo in the 16-bit type (hi = v rounded, lo = the rounded remainder)
+template <typename T>
+__device__ __forceinline__ void split16(float v, uint16_t& hi, uint16_t& lo) {
+  using E = Elem<T>;
+  const T h = E::from_f(v);
+  const T l = E::from_f(v - E::to_f(h));
+  hi = *reinterpret_cast<const uint16_t*>(&h);
+  lo = *reinterpret_cast<const uint16_t*>(&l);
+}
 
 // Per 128-token tile the 2C outputs are produced in two halves of C channels: one
 // MMA of N = 2C (P and G of the half) into one of two 2C-column TMEM accumulators,
-// so the MMA of the next half overlaps the epilogue of the current one.
+// so the MMA of the next half overlaps the epilogue of the current one. The LayerNorm
+// is folded into the GEMM: LN(x) W^T = rstd (x Wc^T - mean sumW + Bc / rstd), the
+// bracket being the x MMAs plus one K step over the per-token statistics (split in
+// 16-bit hi/lo pairs: fp32-exact products, fp32 accumulation), so the epilogue only
+// scales by rstd.
 template <typename T, int C>
 __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
     trimul_in_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                     LnGateArgs a) {
+                     const __grid_constant__ CUtensorMap map_out, LnGateArgs a) {
   using E = Elem<T>;
   using S = TmInSmem<C>;
   constexpr int NOUT = S::NOUT;    // global weight rows: P [0, 2C), G [2C, 4C)
@@ -127,6 +211,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.x_full[s], 1);
       mbar_init(&sm.x_empty[s], 1 + 4);
+      mbar_init(&sm.ext_full[s], 4);
       mbar_init(&sm.st_ready[s], 4);
       mbar_init(&sm.st_free[s], 4 * kInEpiWG);
       mbar_init(&sm.acc_full[s], 1);
@@ -135,11 +220,20 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
     sm.abort = 0;
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < NOUT; i += blockDim.x) {
-    const float sc = i >= 2 * C ? 0.5f : 1.0f;  // sigmoid(g) = 1/2 + tanh(g/2)/2
-    sm.sum_w[i] = a.sum_w[i] * sc;
-    sm.b_const[i] = a.b_const[i] * sc;
+  // the per-channel half of the LayerNorm K step (row n of half hh = output channel)
+  for (int rr = threadIdx.x; rr < 2 * NH; rr += blockDim.x) {
+    const int hh = rr / NH, n = rr % NH, is_g = n >= C;
+    const int gidx = is_g * 2 * C + hh * C + (n - is_g * C);
+    uint16_t sh, sl, bh, bl;
+    split16<T>(a.sum_w[gidx], sh, sl);
+    split16<T>(a.b_const[gidx], bh, bl);
+    uint8_t* rowp = sm.bext[hh];
+    *reinterpret_cast<uint4*>(rowp + sw32_chunk_off(n, 0)) =
+        make_uint4(sh | (static_cast<uint32_t>(sh) << 16), sl | (static_cast<uint32_t>(bh) << 16),
+                   bh | (static_cast<uint32_t>(bl) << 16), 0u);
+    *reinterpret_cast<uint4*>(rowp + sw32_chunk_off(n, 1)) = make_uint4(0u, 0u, 0u, 0u);
   }
+  fence_proxy_async_smem();
   if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
@@ -168,6 +262,10 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
         mbar_expect_tx(&sm.x_full[s], S::TILE);
         for (int ka = 0; ka < KATOMS; ++ka)
           tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.x_full[s], ka * 64, static_cast<int>(tile * 128));
+        // the two-slot ring holds one tile in flight: keep a few more coming into L2
+        const long long pf = tile + TOPS_L2_PREFETCH * static_cast<long long>(gridDim.x);
+        if (TOPS_L2_PREFETCH > 0 && pf < n_tiles)
+          for (int ka = 0; ka < KATOMS; ++ka) tma_prefetch_l2_2d(&map_x, ka * 64, static_cast<int>(pf * 128));
       }
     }
   } else if (warp == 1) {
@@ -196,6 +294,13 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
             mma_ss(tbase + buf * 256, make_smem_desc(xa + off, 16, 1024, kSw128),
                    make_smem_desc(wa + woff, 16, 1024, kSw128), idesc, kk > 0);
           }
+          // the statistics K step, once the tile's statistics are in place
+          if (hh == 0) {
+            if (!mbar_wait(&sm.ext_full[s], (it >> 1) & 1, abort, 409)) { ok = false; break; }
+            tc_fence_after();
+          }
+          mma_ss(tbase + buf * 256, make_smem_desc(smem_u32(sm.aext[s]), 16, 256, kSw32),
+                 make_smem_desc(smem_u32(sm.bext[hh]), 16, 256, kSw32), idesc, 1u);
           mma_commit(&sm.acc_full[buf]);
         }
         if (!ok) break;
@@ -210,25 +315,38 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       if (!mbar_wait(&sm.x_full[s], (it >> 1) & 1, abort, 405)) break;
       float mean, rstd;
       row_stats_kmajor<T, C>(sm.x[s], row, mean, rstd, a.eps);
+      // this token's row of the statistics K step (the slot's previous MMAs are done:
+      // x_full of this tile follows x_empty of the tile two back)
+      uint16_t mh, ml, ih, il;
+      split16<T>(-mean, mh, ml);
+      split16<T>(1.0f / rstd, ih, il);
+      *reinterpret_cast<uint4*>(sm.aext[s] + sw32_chunk_off(row, 0)) =
+          make_uint4(mh | (static_cast<uint32_t>(ml) << 16), mh | (static_cast<uint32_t>(ih) << 16),
+                     il | (static_cast<uint32_t>(ih) << 16), 0u);
+      *reinterpret_cast<uint4*>(sm.aext[s] + sw32_chunk_off(row, 1)) = make_uint4(0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.x_empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&sm.ext_full[s]);
+        mbar_arrive(&sm.x_empty[s]);
+      }
       if (!mbar_wait(&sm.st_free[s], ((it >> 1) & 1) ^ 1, abort, 406)) break;
-      sm.mean[s][row] = mean;
       sm.rstd[s][row] = rstd;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_ready[s]);
     }
   } else if (warp >= 8) {
     // kInEpiWG epilogue warpgroups split the C channels of each half (a warp reaches only
-    // its own 32 TMEM lanes, so the split is by columns); each lane pairs up with its
-    // neighbour token so that every store is one packed 4-byte pair (k, m..m+1)
+    // its own 32 TMEM lanes, so the split is by columns). Each warp stages 8 channels x
+    // its 32 tokens (the D-major layout of ab: one 64-byte row per channel) and stores
+    // them with one TMA box; rows past M are clipped by the TMA unit.
     const int ew = (warp - 8) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const bool odd = lane & 1;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    T* out = static_cast<T*>(a.out);
+    uint16_t* stage = reinterpret_cast<uint16_t*>(sm.stage[warp - 8]);
     bool ok = true;
+    bool staged = false;  // a TMA store of this warp's stage buffer may still be reading it
     int it = 0;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
@@ -236,15 +354,17 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 407)) break;
       TOPS_TCLK(sb2);
       if (lane == 0) TOPS_TADD(2, sa, sb2);
-      const float mean = sm.mean[s][row], rstd = sm.rstd[s][row];
+      const float rstd = sm.rstd[s][row];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_free[s]);
       const long long m = tile * 128 + row;
-      const long long m_even = m & ~1LL;
       float mval = 1.0f;
       if (a.mask != nullptr && m < a.M) mval = static_cast<float>(static_cast<int8_t>(a.mask[m]));
-      // P' = mval * (rstd p + (-mean rstd sumW + Bc));  G/2 = rstd/2 g + (...)/2 (constants pre-halved)
-      const float rp = rstd * mval, rg = 0.5f * rstd, nm = -mean * rstd;
+      // per channel pair (k, k+1), in packed fp32 pairs (acc = x Wc^T - mean sumW + Bc/rstd):
+      //   P' = rstd acc_p;  G/2 = rstd/2 acc_g;  out = (mval/2 + mval/2 tanh(G/2)) P' = mval sigmoid(G) P'
+      const float hm = 0.5f * mval;
+      const unsigned long long rs2 = f2_pack(rstd, rstd), rg2 = f2_pack(0.5f * rstd, 0.5f * rstd);
+      const unsigned long long hm2 = f2_pack(hm, hm);
       for (int hh = 0; hh < 2; ++hh) {
         const int u = 2 * it + hh, buf = u & 1;
         TOPS_TCLK(ea);
@@ -253,44 +373,49 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
         if (lane == 0) TOPS_TADD(0, ea, eb);
         tc_fence_after();
         const uint32_t acc = lane_addr + buf * 256;
-#pragma unroll 1
-        for (int c0 = ew * (C / kInEpiWG); c0 < (ew + 1) * (C / kInEpiWG); c0 += 16) {
-          uint32_t pg[32];  // P then G of 16 channels
-          tmem_ld16x2_async(acc + c0, acc + C + c0, pg);
-          tmem_wait_ld32(pg);
+        // 8-channel steps, each step's TMEM loads issued before the previous step's math
+        constexpr int NSTEP = C / kInEpiWG / 8;
+        const int cbase = ew * (C / kInEpiWG);
+        uint32_t pg[16], nxt[16];  // P then G of 8 channels
+        tmem_ld8x2_async(acc + cbase, acc + C + cbase, pg);
+        tmem_wait_ld16(pg);
 #pragma unroll
-          for (int sub = 0; sub < 16; sub += 8) {
-            // 4 x 8 constants of these channels as 8 broadcast 16-byte shared loads
-            const int kc = hh * C + c0 + sub;
-            float cw[4][8];
-            const float* src[4] = {sm.sum_w + kc, sm.b_const + kc, sm.sum_w + 2 * C + kc, sm.b_const + 2 * C + kc};
+        for (int j = 0; j < NSTEP; ++j) {
+          const int c0 = cbase + 8 * j;
+          const bool more = j + 1 < NSTEP;
+          if (more) tmem_ld8x2_async(acc + c0 + 8, acc + C + c0 + 8, nxt);
+          uint32_t pk[4];  // channel pairs (c0 + 2t, c0 + 2t + 1) of this token
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+          for (int t = 0; t < 4; ++t) {
+            const unsigned long long pv = f2_mul(rs2, f2_pack(__uint_as_float(pg[2 * t]), __uint_as_float(pg[2 * t + 1])));
+            const unsigned long long gh =
+                f2_mul(rg2, f2_pack(__uint_as_float(pg[8 + 2 * t]), __uint_as_float(pg[8 + 2 * t + 1])));
+            float g0, g1;
+            f2_unpack(gh, g0, g1);
+            const unsigned long long v = f2_mul(f2_fma(f2_pack(tanh_approx(g0), tanh_approx(g1)), hm2, hm2), pv);
+            float v0, v1;
+            f2_unpack(v, v0, v1);
+            pk[t] = E::pack2(v0, v1);
+          }
+          // stage the 8 channels (once the previous box has left the buffer) and store them
+          if (staged && lane == 0) bulk_wait_read0();
+          __syncwarp();
 #pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const float4 f = reinterpret_cast<const float4*>(src[q])[i];
-                cw[q][4 * i] = f.x;
-                cw[q][4 * i + 1] = f.y;
-                cw[q][4 * i + 2] = f.z;
-                cw[q][4 * i + 3] = f.w;
-              }
+          for (int t = 0; t < 4; ++t) {
+            stage[(2 * t) * 32 + lane] = static_cast<uint16_t>(pk[t] & 0xFFFFu);
+            stage[(2 * t + 1) * 32 + lane] = static_cast<uint16_t>(pk[t] >> 16);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_out, stage, static_cast<int>(tile * 128 + wq * 32), hh * C + c0);
+            bulk_commit();
+          }
+          staged = true;
+          if (more) {
+            tmem_wait_ld16(nxt);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              float v[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int i = e + h;
-                const float pv = fmaf(rp, __uint_as_float(pg[sub + i]), mval * fmaf(nm, cw[0][i], cw[1][i]));
-                const float gh = fmaf(rg, __uint_as_float(pg[16 + sub + i]), fmaf(nm, cw[2][i], cw[3][i]));
-                v[h] = fmaf(0.5f, tanh_approx(gh), 0.5f) * pv;
-              }
-              // even lane: stores channel k for tokens (m, m+1); odd lane: channel k+1 for (m-1, m)
-              const float other = __shfl_xor_sync(0xffffffffu, odd ? v[0] : v[1], 1);
-              const uint32_t pk = odd ? E::pack2(other, v[1]) : E::pack2(v[0], other);
-              // M is even (the C ABI checks it), so a token pair is either whole or past the end
-              const int k = kc + e + (odd ? 1 : 0);
-              if (m < a.M) *reinterpret_cast<uint32_t*>(out + static_cast<long long>(k) * a.M + m_even) = pk;
-            }
+            for (int t = 0; t < 16; ++t) pg[t] = nxt[t];
           }
         }
         tc_fence_before();
@@ -300,6 +425,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
         if (lane == 0) TOPS_TADD(1, eb, ec);
       }
     }
+    if (lane == 0) bulk_wait0();
   }
   TOPS_TFLUSH();
   tc_fence_before();
@@ -537,6 +663,12 @@ __global__ void __launch_bounds__(512, 1)
         const int m0 = static_cast<int>(tile * 128);
         for (int h = 0; h < 2; ++h) tma_load_2d(sm.y[s] + h * C * 128, &map_y, &sm.in_full[s], m0 + h * 64, 0);
         for (int ka = 0; ka < KATOMS; ++ka) tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.in_full[s], ka * 64, m0);
+        const long long pf = tile + TOPS_L2_PREFETCH * static_cast<long long>(gridDim.x);
+        if (TOPS_L2_PREFETCH > 0 && pf < n_tiles) {
+          const int p0 = static_cast<int>(pf * 128);
+          for (int h = 0; h < 2; ++h) tma_prefetch_l2_2d(&map_y, p0 + h * 64, 0);
+          for (int ka = 0; ka < KATOMS; ++ka) tma_prefetch_l2_2d(&map_x, ka * 64, p0);
+        }
       }
     }
   } else if (warp == 1) {
@@ -573,13 +705,13 @@ __global__ void __launch_bounds__(512, 1)
       const int s = it & 1;
       if (!mbar_wait(&sm.in_full[s], (it >> 1) & 1, abort, 605)) break;
       float my, ry, mx, rx;
-      col_stats_mnmajor<T, C>(sm.y[s], row, my, ry, a.eps);
+      const int ytok = col_stats_coop<T, C>(sm.y[s], row, my, ry, a.eps);
       row_stats_kmajor<T, C>(sm.x[s], row, mx, rx, a.eps);
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.in_empty[s]);
       if (!mbar_wait(&sm.st_free[s], ((it >> 1) & 1) ^ 1, abort, 606)) break;
-      sm.st[s][0][row] = my;
-      sm.st[s][1][row] = ry;
+      sm.st[s][0][ytok] = my;
+      sm.st[s][1][ytok] = ry;
       sm.st[s][2][row] = mx;
       sm.st[s][3][row] = rx;
       __syncwarp();
