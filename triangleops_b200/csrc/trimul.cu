@@ -184,6 +184,30 @@ __device__ __forceinline__ void split16(float v, uint16_t& hi, uint16_t& lo) {
   lo = *reinterpret_cast<const uint16_t*>(&l);
 }
 
+// this token's row of a statistics K step: [-mean hi, -mean lo, -mean hi, 1/rstd hi, 1/rstd lo, 1/rstd hi, 0...]
+template <typename T>
+__device__ __forceinline__ void write_stats_row(uint8_t* tile, int row, float mean, float rstd) {
+  uint16_t mh, ml, ih, il;
+  split16<T>(-mean, mh, ml);
+  split16<T>(1.0f / rstd, ih, il);
+  *reinterpret_cast<uint4*>(tile + sw32_chunk_off(row, 0)) =
+      make_uint4(mh | (static_cast<uint32_t>(ml) << 16), mh | (static_cast<uint32_t>(ih) << 16),
+                 il | (static_cast<uint32_t>(ih) << 16), 0u);
+  *reinterpret_cast<uint4*>(tile + sw32_chunk_off(row, 1)) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// an output channel's row of a statistics K step: [sumW hi, sumW hi, sumW lo, Bc hi, Bc hi, Bc lo, 0...]
+template <typename T>
+__device__ __forceinline__ void write_const_row(uint8_t* tile, int row, float sum_w, float b_const) {
+  uint16_t sh, sl, bh, bl;
+  split16<T>(sum_w, sh, sl);
+  split16<T>(b_const, bh, bl);
+  *reinterpret_cast<uint4*>(tile + sw32_chunk_off(row, 0)) =
+      make_uint4(sh | (static_cast<uint32_t>(sh) << 16), sl | (static_cast<uint32_t>(bh) << 16),
+                 bh | (static_cast<uint32_t>(bl) << 16), 0u);
+  *reinterpret_cast<uint4*>(tile + sw32_chunk_off(row, 1)) = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // Per 128-token tile the 2C outputs are produced in two halves of C channels: one
 // MMA of N = 2C (P and G of the half) into one of two 2C-column TMEM accumulators,
 // so the MMA of the next half overlaps the epilogue of the current one. The LayerNorm
@@ -224,14 +248,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
   for (int rr = threadIdx.x; rr < 2 * NH; rr += blockDim.x) {
     const int hh = rr / NH, n = rr % NH, is_g = n >= C;
     const int gidx = is_g * 2 * C + hh * C + (n - is_g * C);
-    uint16_t sh, sl, bh, bl;
-    split16<T>(a.sum_w[gidx], sh, sl);
-    split16<T>(a.b_const[gidx], bh, bl);
-    uint8_t* rowp = sm.bext[hh];
-    *reinterpret_cast<uint4*>(rowp + sw32_chunk_off(n, 0)) =
-        make_uint4(sh | (static_cast<uint32_t>(sh) << 16), sl | (static_cast<uint32_t>(bh) << 16),
-                   bh | (static_cast<uint32_t>(bl) << 16), 0u);
-    *reinterpret_cast<uint4*>(rowp + sw32_chunk_off(n, 1)) = make_uint4(0u, 0u, 0u, 0u);
+    write_const_row<T>(sm.bext[hh], n, a.sum_w[gidx], a.b_const[gidx]);
   }
   fence_proxy_async_smem();
   if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
@@ -317,13 +334,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       row_stats_kmajor<T, C>(sm.x[s], row, mean, rstd, a.eps);
       // this token's row of the statistics K step (the slot's previous MMAs are done:
       // x_full of this tile follows x_empty of the tile two back)
-      uint16_t mh, ml, ih, il;
-      split16<T>(-mean, mh, ml);
-      split16<T>(1.0f / rstd, ih, il);
-      *reinterpret_cast<uint4*>(sm.aext[s] + sw32_chunk_off(row, 0)) =
-          make_uint4(mh | (static_cast<uint32_t>(ml) << 16), mh | (static_cast<uint32_t>(ih) << 16),
-                     il | (static_cast<uint32_t>(ih) << 16), 0u);
-      *reinterpret_cast<uint4*>(sm.aext[s] + sw32_chunk_off(row, 1)) = make_uint4(0u, 0u, 0u, 0u);
+      write_stats_row<T>(sm.aext[s], row, mean, rstd);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -599,16 +610,27 @@ __global__ void __launch_bounds__(384, 1)
 // ===========================================================================
 // output phase
 // ===========================================================================
+// output phase warp roles after the producer / MMA warps (0-3): kOutStatWG statistics
+// warpgroups, then kOutEpiWG epilogue warpgroups (kOutStatWG + kOutEpiWG = 3: 512 threads)
+#ifndef TOPS_OUT_STAT_WG
+#define TOPS_OUT_STAT_WG 2
+#endif
+constexpr int kOutStatWG = TOPS_OUT_STAT_WG;
+constexpr int kOutEpiWG = 3 - kOutStatWG;
+
 template <int C>
 struct TmOutSmem {
   static constexpr int TILE = (C / 64) * 16384;
   alignas(1024) uint8_t w[2 * (C / 64) * C * 128];  // p_out rows [0,C), g_out rows [C,2C); per K atom
   alignas(1024) uint8_t y[2][TILE];                 // MN-major: two 64-token halves x C rows
   alignas(1024) uint8_t x[2][TILE];                 // K-major
-  float st[2][4][128];                              // mean_y, rstd_y, mean_x, rstd_x
-  alignas(16) float sum_w[2 * C];                   // folded LN constants (p_out | g_out)
-  alignas(16) float b_const[2 * C];
-  uint64_t bar_w, in_full[2], in_empty[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
+  // the two LayerNorms as one more K step each (K-major, 32-byte swizzle), as in the
+  // input phase: per token [-mean hi, -mean lo, -mean hi, 1/rstd hi, 1/rstd lo, 1/rstd hi]
+  // of y (P) and of x (G), against per output channel [sumW hi, sumW hi, sumW lo, Bc hi, Bc hi, Bc lo]
+  alignas(1024) uint8_t aext[2][2][128 * 32];        // [slot][y | x]
+  alignas(1024) uint8_t bext[2][C * 32];             // [p_out | g_out]
+  float st[2][2][128];                               // rstd_y, rstd_x
+  uint64_t bar_w, in_full[2], in_empty[2], ext_full[2], st_ready[2], st_free[2], acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -628,20 +650,18 @@ __global__ void __launch_bounds__(512, 1)
     mbar_init(&sm.bar_w, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.in_full[s], 1);
-      mbar_init(&sm.in_empty[s], 1 + 4);
-      mbar_init(&sm.st_ready[s], 4);
-      mbar_init(&sm.st_free[s], 8);
+      mbar_init(&sm.in_empty[s], 1 + 4 * kOutStatWG);
+      mbar_init(&sm.ext_full[s], 4 * kOutStatWG);
+      mbar_init(&sm.st_ready[s], 4 * kOutStatWG);
+      mbar_init(&sm.st_free[s], 4 * kOutEpiWG);
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_empty[s], 8);
+      mbar_init(&sm.acc_empty[s], 4 * kOutEpiWG);
     }
     sm.abort = 0;
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) {
-    const float sc = i >= C ? 0.5f : 1.0f;  // G half pre-scaled for the tanh form of the sigmoid
-    sm.sum_w[i] = a.sum_w[i] * sc;
-    sm.b_const[i] = a.b_const[i] * sc;
-  }
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) write_const_row<T>(sm.bext[i / C], i % C, a.sum_w[i], a.b_const[i]);
+  fence_proxy_async_smem();
   if (warp == 1) tmem_alloc(&sm.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
@@ -694,32 +714,49 @@ __global__ void __launch_bounds__(512, 1)
           mma_ss(acc + C, make_smem_desc(xa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
                  make_smem_desc(wa + woff + C * 128, 16, 1024, kSw128), id_x, kk > 0);
         }
+        // the LayerNorm K steps (K-major), once the tile's statistics are in place
+        if (!mbar_wait(&sm.ext_full[s], (it >> 1) & 1, abort, 609)) break;
+        tc_fence_after();
+        mma_ss(acc, make_smem_desc(smem_u32(sm.aext[s][0]), 16, 256, kSw32),
+               make_smem_desc(smem_u32(sm.bext[0]), 16, 256, kSw32), id_x, 1u);
+        mma_ss(acc + C, make_smem_desc(smem_u32(sm.aext[s][1]), 16, 256, kSw32),
+               make_smem_desc(smem_u32(sm.bext[1]), 16, 256, kSw32), id_x, 1u);
         mma_commit(&sm.in_empty[s]);
         mma_commit(&sm.acc_full[s]);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    const int row = (warp - 4) * 32 + lane;
+  } else if (warp >= 4 && warp < 4 + 4 * kOutStatWG) {
+    // statistics: one warpgroup for both LayerNorms, or one for y and one for x
+    const bool do_y = kOutStatWG == 1 || warp < 8, do_x = kOutStatWG == 1 || warp >= 8;
+    const int row = (warp & 3) * 32 + lane;
     int it = 0;
     for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       if (!mbar_wait(&sm.in_full[s], (it >> 1) & 1, abort, 605)) break;
-      float my, ry, mx, rx;
-      const int ytok = col_stats_coop<T, C>(sm.y[s], row, my, ry, a.eps);
-      row_stats_kmajor<T, C>(sm.x[s], row, mx, rx, a.eps);
+      float my = 0.f, ry = 1.f, mx = 0.f, rx = 1.f;
+      int ytok = row;
+      if (do_y) ytok = col_stats_coop<T, C>(sm.y[s], row, my, ry, a.eps);
+      if (do_x) row_stats_kmajor<T, C>(sm.x[s], row, mx, rx, a.eps);
+      // the slot's statistics rows (its previous MMAs are done: in_full of this tile
+      // follows in_empty of the tile two back)
+      if (do_y) write_stats_row<T>(sm.aext[s][0], ytok, my, ry);
+      if (do_x) write_stats_row<T>(sm.aext[s][1], row, mx, rx);
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.in_empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&sm.ext_full[s]);
+        mbar_arrive(&sm.in_empty[s]);
+      }
       if (!mbar_wait(&sm.st_free[s], ((it >> 1) & 1) ^ 1, abort, 606)) break;
-      sm.st[s][0][ytok] = my;
-      sm.st[s][1][ytok] = ry;
-      sm.st[s][2][row] = mx;
-      sm.st[s][3][row] = rx;
+      if (do_y) sm.st[s][0][ytok] = ry;
+      if (do_x) sm.st[s][1][row] = rx;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_ready[s]);
     }
-  } else if (warp >= 8) {
-    // two epilogue warpgroups split the C output columns of every tile
-    const int ew = (warp - 8) >> 2;
+  } else if (warp >= 4 + 4 * kOutStatWG) {
+    // kOutEpiWG epilogue warpgroups split the C output columns of every tile
+    constexpr int CW = C / kOutEpiWG;
+    const int ew = (warp - 4 - 4 * kOutStatWG) >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
@@ -727,7 +764,7 @@ __global__ void __launch_bounds__(512, 1)
     for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 607)) break;
-      const float my = sm.st[s][0][row], ry = sm.st[s][1][row], mx = sm.st[s][2][row], rx = sm.st[s][3][row];
+      const float ry = sm.st[s][0][row], rx = sm.st[s][1][row];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_free[s]);
       if (!mbar_wait(&sm.acc_full[s], (it >> 1) & 1, abort, 608)) break;
@@ -735,14 +772,17 @@ __global__ void __launch_bounds__(512, 1)
       const long long m = tile * 128 + row;
       T* dst = static_cast<T*>(a.out) + m * C;
       const T* res = a.residual != nullptr ? static_cast<const T*>(a.residual) + m * C : nullptr;
-      const float nmy = -my * ry, nmx = -mx * rx, rxh = 0.5f * rx;
+      // acc = z Wc^T - mean sumW + Bc / rstd for z = y (P) and x (G):
+      //   P' = rstd_y acc_p;  G/2 = rstd_x/2 acc_g;  out = (1/2 + 1/2 tanh(G/2)) P' (+ residual)
+      const unsigned long long ry2 = f2_pack(ry, ry), rx2 = f2_pack(0.5f * rx, 0.5f * rx);
+      const unsigned long long half2 = f2_pack(0.5f, 0.5f);
       const uint32_t acc = lane_addr + s * 256;
       // chunk loads (P then G of 16 columns) one chunk ahead of the math
       uint32_t pg[32], nxt[32];
-      tmem_ld16x2_async(acc + ew * (C / 2), acc + C + ew * (C / 2), pg);
+      tmem_ld16x2_async(acc + ew * CW, acc + C + ew * CW, pg);
       tmem_wait_ld32(pg);
-      for (int c0 = ew * (C / 2); c0 < (ew + 1) * (C / 2); c0 += 16) {
-        const bool more = c0 + 16 < (ew + 1) * (C / 2);
+      for (int c0 = ew * CW; c0 < (ew + 1) * CW; c0 += 16) {
+        const bool more = c0 + 16 < (ew + 1) * CW;
         if (more) tmem_ld16x2_async(acc + c0 + 16, acc + C + c0 + 16, nxt);
         if (m < a.M) {
 #pragma unroll
@@ -756,35 +796,20 @@ __global__ void __launch_bounds__(512, 1)
               rs[2] = u.z;
               rs[3] = u.w;
             }
-            float cw[4][8];
-            const float* src[4] = {sm.sum_w + cc, sm.b_const + cc, sm.sum_w + C + cc, sm.b_const + C + cc};
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const float4 f = reinterpret_cast<const float4*>(src[q])[i];
-                cw[q][4 * i] = f.x;
-                cw[q][4 * i + 1] = f.y;
-                cw[q][4 * i + 2] = f.z;
-                cw[q][4 * i + 3] = f.w;
-              }
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float v[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int i = 2 * e + h;
-                const float pv = fmaf(ry, __uint_as_float(pg[sub + i]), fmaf(nmy, cw[0][i], cw[1][i]));
-                // G constants pre-halved: sigmoid(g) = 1/2 + tanh(g/2)/2
-                const float gh = fmaf(rxh, __uint_as_float(pg[16 + sub + i]), fmaf(nmx, cw[2][i], cw[3][i]));
-                v[h] = fmaf(0.5f, tanh_approx(gh), 0.5f) * pv;
-              }
-              if (res != nullptr) {
-                v[0] += E::lo(rs[e]);
-                v[1] += E::hi(rs[e]);
-              }
-              o[e] = E::pack2(v[0], v[1]);
+              const int i = sub + 2 * e;
+              const unsigned long long pv = f2_mul(ry2, f2_pack(__uint_as_float(pg[i]), __uint_as_float(pg[i + 1])));
+              const unsigned long long gh =
+                  f2_mul(rx2, f2_pack(__uint_as_float(pg[16 + i]), __uint_as_float(pg[16 + i + 1])));
+              float g0, g1;
+              f2_unpack(gh, g0, g1);
+              unsigned long long v = f2_mul(f2_fma(f2_pack(tanh_approx(g0), tanh_approx(g1)), half2, half2), pv);
+              if (res != nullptr) v = f2_add(v, f2_pack(E::lo(rs[e]), E::hi(rs[e])));
+              float v0, v1;
+              f2_unpack(v, v0, v1);
+              o[e] = E::pack2(v0, v1);
             }
             *reinterpret_cast<uint4*>(dst + cc) = make_uint4(o[0], o[1], o[2], o[3]);
           }
