@@ -134,6 +134,9 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+#ifndef TOPS_L2_PREFETCH
+#define TOPS_L2_PREFETCH 4  // tiles ahead that the streaming kernels prefetch into L2 (0: off)
+#endif
 // Tiled prefetch of a box into L2 (no shared memory, no barrier): a later TMA load of
 // the same box then hits L2. Lets a kernel whose shared-memory ring is shallow keep
 // more bytes in flight from HBM.

@@ -16,10 +16,6 @@
 
 namespace tops {
 
-#ifndef TOPS_L2_PREFETCH
-#define TOPS_L2_PREFETCH 4  // tiles ahead that the streaming phases prefetch into L2 (0: off)
-#endif
-
 struct LnGateArgs {
   long long M;           // tokens
   float eps;
