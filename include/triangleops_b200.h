@@ -180,7 +180,7 @@ int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t Mq, int64_t 
  * allocate device memory (a serving runtime or embedding framework that owns a
  * fixed device-memory budget and forbids allocation after start-up): same
  * arguments minus the five workspaces, which live in one library-owned static
- * device array of about 4.6 MB per GPU, held until process exit. Limits: M <= 512,
+ * device array of about 2.5 MB per GPU, held until process exit. Limits: M <= 512,
  * C = 128, H = 4, D = 32, Cz = 128; M > 512 returns TOPS_ERR_CAPACITY. The array
  * is shared by all calls on a device — calls that overlap on the GPU race. The
  * first call on a device looks up the array's address; make it before any stream

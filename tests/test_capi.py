@@ -102,7 +102,7 @@ def test_workspace_bytes_match_the_python_layer():
     M, Mq = 200, 100
     mp = (M + 7) // 8 * 8
     assert lib.tops_apb_workspace_bytes(I64(M), I64(Mq), I64(H), I64(D), out) == 0
-    assert list(out)[:5] == [H * M * D * 2, H * M * D * 2, H * D * mp * 2, mp * 2, H * Mq * mp * 4]
+    assert list(out)[:5] == [H * M * D * 2, H * M * D * 2, H * D * mp * 2, mp * 2, H * Mq * mp * 2]
     assert lib.tops_apb_workspace_bytes(I64(M), I64(M + 1), I64(H), I64(D), out) == _lib.ERR_SHAPE
     assert lib.tops_apb_workspace_bytes(I64(M), I64(M), I64(H), I64(D), None) == _lib.ERR_ARG
 

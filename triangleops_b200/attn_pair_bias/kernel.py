@@ -50,8 +50,8 @@ def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, sca
     q = torch.empty(1, H, M, D, dtype=torch.float16, device=dev)
     k = torch.empty(1, H, M, D, dtype=torch.float16, device=dev)
     vt = torch.empty(1, H, D, mkp, dtype=torch.float16, device=dev)
-    maskf = torch.empty(1, mkp, dtype=torch.float16, device=dev)
-    bias = torch.empty(H, Mq, mkp, dtype=torch.float32, device=dev)
+    pen = torch.empty(1, mkp, dtype=torch.float16, device=dev) if key_mask is not None else None
+    bias = torch.empty(H, Mq, mkp, dtype=torch.float16, device=dev)  # logits in log2 units
     km = None
     if key_mask is not None:
         km = key_mask.reshape(M)
@@ -66,7 +66,7 @@ def apb_core(X, w_rows, Z, W_combined, sum_W_combined, B_const, Og, H, D, *, sca
     dst = Og if Og.is_contiguous() else torch.empty(Mq, H * D, dtype=X.dtype, device=dev)
     _lib.call("tops_apb_forward_rows", dt, M, q0, Mq, C, Z.shape[-1], H, D, X.data_ptr(), w_rows.data_ptr(),
               Z.data_ptr(), wc.data_ptr(), sw.data_ptr(), bc.data_ptr(), _lib.ptr(km), float(scale), float(eps), q.data_ptr(),
-              k.data_ptr(), vt.data_ptr(), maskf.data_ptr(), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(dev))
+              k.data_ptr(), vt.data_ptr(), _lib.ptr(pen), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(dev))
     if dst is not Og:
         Og.copy_(dst)
     return Og

@@ -23,37 +23,39 @@ using namespace tops;
 extern "C" int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t Mq, int64_t C, int64_t Cz, int64_t H,
                                      int64_t D, const void* x, const void* w_qkv, const void* z_rows, const float* wc,
                                      const float* sum_w, const float* b_const, const uint8_t* key_mask, float scale,
-                                     float eps, void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws,
+                                     float eps, void* q_ws, void* k_ws, void* vt_ws, void* pen_ws, void* bias_ws,
                                      void* og_rows, void* stream) {
   if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
   if (M <= 0 || M >= (1 << 20) || Cz != 128 || H != 4 || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
   if (q0 < 0 || Mq <= 0 || q0 + Mq > M) return TOPS_ERR_SHAPE;
-  const void* ptrs[] = {x, w_qkv, z_rows, wc, sum_w, b_const, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, og_rows};
+  const void* ptrs[] = {x, w_qkv, z_rows, wc, sum_w, b_const, q_ws, k_ws, vt_ws, bias_ws, og_rows};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  if (key_mask != nullptr && (pen_ws == nullptr || !aligned16(pen_ws))) return TOPS_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), mq = static_cast<int>(Mq);
   const int mkp = (m + 7) & ~7;
-  ZBiasArgs za{static_cast<long long>(Mq) * M, m, mkp, mq, eps, wc, sum_w, b_const, static_cast<float*>(bias_ws)};
+  ZBiasArgs za{static_cast<long long>(Mq) * M, m, mkp, mq, eps, wc, sum_w, b_const, static_cast<__half*>(bias_ws)};
   int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(z_rows, za, st) : launch_zbias<__half>(z_rows, za, st);
   if (rc != TOPS_OK) return rc;
   // Q/K/V projection of the whole (replicated, M x C) sequence: K/V are needed for
   // every key, and Q for all M rows costs less than a gather of the window; the
-  // key mask zeroes V rows and feeds the row-sum column of the PV MMA.
-  ProjArgs pa{m, m, 1, mkp, scale * kLog2e, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, maskf_ws,
+  // key mask becomes the penalty row (0 / -inf) the attention adds to every score.
+  void* pen = key_mask != nullptr ? pen_ws : nullptr;
+  ProjArgs pa{m, m, 1, mkp, scale * kLog2e, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, pen,
               nullptr};
   rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), false, false, x, w_qkv, pa, st);
   if (rc != TOPS_OK) return rc;
   // attention of query rows [q0, q0 + Mq): a row window of Q ([H][M][D], f16)
   const void* q_win = static_cast<const char*>(q_ws) + q0 * D * 2;
-  return run_attn<1, 2, true>(dtype, static_cast<int>(D), 1, static_cast<int>(H), mq, m, mkp, q_win, k_ws, vt_ws,
-                              maskf_ws, bias_ws, og_rows, st, m);
+  return run_attn<1>(dtype, static_cast<int>(D), 1, static_cast<int>(H), mq, m, mkp, q_win, k_ws, vt_ws, pen, bias_ws,
+                     og_rows, st, m);
 }
 
 extern "C" int tops_apb_forward(int dtype, int64_t M, int64_t C, int64_t Cz, int64_t H, int64_t D, const void* x,
                                 const void* w_qkv, const void* z, const float* wc, const float* sum_w,
                                 const float* b_const, const uint8_t* key_mask, float scale, float eps, void* q_ws,
-                                void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws, void* og_out, void* stream) {
+                                void* k_ws, void* vt_ws, void* pen_ws, void* bias_ws, void* og_out, void* stream) {
   return tops_apb_forward_rows(dtype, M, 0, M, C, Cz, H, D, x, w_qkv, z, wc, sum_w, b_const, key_mask, scale, eps,
-                               q_ws, k_ws, vt_ws, maskf_ws, bias_ws, og_out, stream);
+                               q_ws, k_ws, vt_ws, pen_ws, bias_ws, og_out, stream);
 }

@@ -86,75 +86,78 @@ int run_proj(int dtype, int C, int D, bool ln, bool bp, const void* x, const voi
 // ---------------------------------------------------------------------------
 // attention
 // ---------------------------------------------------------------------------
-template <typename T, int D, int TR, int TQ, bool BF32>
-int launch_attn(int dtype, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
-                const void* maskf, const void* bias, void* out, cudaStream_t st, int q_head_rows) {
-  using Cfg = AttnCfg<D, TR, TQ, BF32>;
-  const CUtensorMapDataType dt = tmap_dtype(dtype);
+template <typename T, int D, int TR>
+int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt, const void* pen,
+                const void* bias, void* out, cudaStream_t st, int q_head_rows) {
+  using Cfg = AttnCfg<D, TR>;
   const CUtensorMapSwizzle qk_sw = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  CUtensorMap mq, mk, mv, mm, mb;
+  const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap mq, mk, mv, mp, mb;
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nq), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(q_head_rows) * D * 2};
     const uint32_t box[3] = {D, 128, 1};
-    if (!make_tmap(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mq, f16, 3, q, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Nk), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(Nk) * D * 2};
     const uint32_t box[3] = {D, Cfg::BK, 1};
-    if (!make_tmap(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, k, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
+    if (!make_tmap(&mk, f16, 3, k, dims, str, box, qk_sw)) return TOPS_ERR_TMAP;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(D), static_cast<uint64_t>(R) * H};
     const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * D * 2};
     const uint32_t box[3] = {Cfg::BK, D, 1};
-    if (!make_tmap(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vt, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
-      return TOPS_ERR_TMAP;
+    if (!make_tmap(&mv, f16, 3, vt, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
-  {
+  if (pen != nullptr) {
     const uint64_t dims[2] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(R)};
     const uint64_t str[1] = {static_cast<uint64_t>(Nkp) * 2};
     const uint32_t box[2] = {Cfg::BK, 1};
-    if (!make_tmap(&mm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, maskf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
-      return TOPS_ERR_TMAP;
+    if (!make_tmap(&mp, f16, 2, pen, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return TOPS_ERR_TMAP;
+  } else {
+    mp = mv;  // unused (has_mask = 0)
   }
   {
-    const uint64_t eb = BF32 ? 4 : 2;
     const uint64_t dims[3] = {static_cast<uint64_t>(Nk), static_cast<uint64_t>(Nq), static_cast<uint64_t>(H)};
-    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * eb, static_cast<uint64_t>(Nkp) * Nq * eb};
-    const uint32_t box[3] = {BF32 ? 32u : static_cast<uint32_t>(Cfg::BK), 128, 1};
-    if (!make_tmap(&mb, BF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, bias, dims, str, box,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
-      return TOPS_ERR_TMAP;
+    const uint64_t str[2] = {static_cast<uint64_t>(Nkp) * 2, static_cast<uint64_t>(Nkp) * Nq * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(Cfg::BK), 128, 1};
+    if (!make_tmap(&mb, f16, 3, bias, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
-  AttnArgs args{R, Nq, Nk, out, H};
-  const size_t smem = sizeof(AttnSmem<D, TR, TQ, BF32>) + 1024;
-  auto kern = attn_kernel<T, D, TR, TQ, BF32>;
+  AttnArgs args{R, Nq, Nk, out, H, pen != nullptr ? 1 : 0};
+  const size_t smem = sizeof(AttnSmem<D, TR>) + 1024;
+  auto kern = attn_kernel<T, D, TR>;
   set_smem(kern, smem);
   // persistent: one CTA per SM (shared memory and TMEM allow no second), looping over units
-  const long long units = static_cast<long long>((Nq + 128 * TQ - 1) / (128 * TQ)) * ((R + TR - 1) / TR) * H;
+  const long long units = static_cast<long long>((Nq + 127) / 128) * ((R + TR - 1) / TR) * H;
   const int grid = units < sm_count() ? static_cast<int>(units) : sm_count();
-  kern<<<grid, Cfg::THREADS, smem, st>>>(mq, mk, mv, mm, mb, args);
+  kern<<<grid, Cfg::THREADS, smem, st>>>(mq, mk, mv, mp, mb, args);
+  if (cudaGetLastError() != cudaSuccess) return TOPS_ERR_CUDA;
+  if (pen != nullptr) {
+    // rows whose keys are all masked (rare: one vote per row, work only for dead rows)
+    const int grid_d = R < 4 * sm_count() ? R : 4 * sm_count();
+    attn_deadrow_kernel<T><<<grid_d, 128, 0, st>>>(static_cast<const __half*>(pen), static_cast<const __half*>(vt),
+                                                   static_cast<T*>(out), R, Nq, Nk, Nkp, H * D);
+  }
   return launch_status();
 }
 
 // TR rows share one bias tile (TR > 1 only pays off when many rows share the bias).
-template <int TR, int TQ, bool BF32 = false>
+// pen: the [R][Nkp] f16 key-penalty rows (0 / -inf), or NULL when no key is masked.
+template <int TR>
 int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
-             const void* maskf, const void* bias, void* out, cudaStream_t st, int q_head_rows = 0) {
+             const void* pen, const void* bias, void* out, cudaStream_t st, int q_head_rows = 0) {
   // q_head_rows: rows per head of the Q buffer (Q may be a row window of a longer
   // [R][H][q_head_rows][D] array, q pointing at its first row); 0 means Nq.
   if (q_head_rows == 0) q_head_rows = Nq;
   if (q_head_rows < Nq) return TOPS_ERR_SHAPE;
   if (dtype == TOPS_BF16) {
-    if (D == 32)
-      return launch_attn<__nv_bfloat16, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
-    if (D == 16)
-      return launch_attn<__nv_bfloat16, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
+    if (D == 32) return launch_attn<__nv_bfloat16, 32, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 16) return launch_attn<__nv_bfloat16, 16, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
   } else if (dtype == TOPS_F16) {
-    if (D == 32) return launch_attn<__half, 32, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
-    if (D == 16) return launch_attn<__half, 16, TR, TQ, BF32>(dtype, R, H, Nq, Nk, Nkp, q, k, vt, maskf, bias, out, st, q_head_rows);
+    if (D == 32) return launch_attn<__half, 32, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 16) return launch_attn<__half, 16, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
   }
   return TOPS_ERR_SHAPE;
 }
@@ -203,20 +206,23 @@ using namespace tops;
 
 static int project_impl(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D, const void* x, int apply_ln,
                         const float* ln_w, const float* ln_b, const void* w_qkvz, const float* bz, const uint8_t* mask,
-                        float scale, float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws,
+                        float scale, float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws, void* pen_ws,
                         void* bias_ws, void* stream, int trans) {
   if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
   if (N <= 0 || R <= 0 || R > N || !attn_shape_ok(C, H, D)) return TOPS_ERR_SHAPE;
   if (R * N >= (int64_t(1) << 31)) return TOPS_ERR_SHAPE;
   if (apply_ln && (ln_w == nullptr || ln_b == nullptr)) return TOPS_ERR_ARG;
-  const void* ptrs[] = {x, w_qkvz, bz, q_ws, k_ws, vt_ws, maskf_ws, bias_ws};
+  const void* ptrs[] = {x, w_qkvz, bz, q_ws, k_ws, vt_ws, bias_ws};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   if (xln_ws != nullptr && !aligned16(xln_ws)) return TOPS_ERR_ALIGN;
+  // the penalty rows are written only for a masked call (and then required)
+  if (mask != nullptr && (pen_ws == nullptr || !aligned16(pen_ws))) return TOPS_ERR_ALIGN;
+  if (mask == nullptr) pen_ws = nullptr;
   const int n = static_cast<int>(N), r = static_cast<int>(R);
   const int nkp = (n + 7) & ~7;
   ProjArgs pa{r * n, n, r, nkp, scale * kLog2e, eps, ln_w, ln_b, bz, mask, apply_ln ? xln_ws : nullptr,
-              q_ws, k_ws, vt_ws, maskf_ws, bias_ws, trans};
+              q_ws, k_ws, vt_ws, pen_ws, bias_ws, trans};
   return run_proj(dtype, static_cast<int>(C), static_cast<int>(D), apply_ln != 0, true, x, w_qkvz, pa,
                   static_cast<cudaStream_t>(stream));
 }
@@ -225,44 +231,46 @@ extern "C" int tops_triangle_attn_project(int dtype, int64_t R, int64_t N, int64
                                           const void* x, int apply_ln, const float* ln_w, const float* ln_b,
                                           const void* w_qkvz, const float* bz, const uint8_t* mask, float scale,
                                           float eps, void* xln_ws, void* q_ws, void* k_ws, void* vt_ws,
-                                          void* maskf_ws, void* bias_ws, void* stream) {
+                                          void* pen_ws, void* bias_ws, void* stream) {
   return project_impl(dtype, R, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps, xln_ws, q_ws, k_ws,
-                      vt_ws, maskf_ws, bias_ws, stream, 0);
+                      vt_ws, pen_ws, bias_ws, stream, 0);
 }
 
 extern "C" int tops_triangle_attn_project_transposed(int dtype, int64_t R, int64_t N, int64_t C, int64_t H,
                                                      int64_t D, const void* x, int apply_ln, const float* ln_w,
                                                      const float* ln_b, const void* w_qkvz, const float* bz,
                                                      const uint8_t* mask, float scale, float eps, void* xln_ws,
-                                                     void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws,
+                                                     void* q_ws, void* k_ws, void* vt_ws, void* pen_ws,
                                                      void* bias_ws, void* stream) {
   if (N % 8 != 0) return TOPS_ERR_ALIGN;  // the column stride N*C*2 bytes must be a multiple of 16
   return project_impl(dtype, R, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps, xln_ws, q_ws, k_ws,
-                      vt_ws, maskf_ws, bias_ws, stream, 1);
+                      vt_ws, pen_ws, bias_ws, stream, 1);
 }
 
 extern "C" int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_t H, int64_t D, const void* q_ws,
-                                         const void* k_ws, const void* vt_ws, const void* maskf_ws,
+                                         const void* k_ws, const void* vt_ws, const void* pen_ws,
                                          const void* bias_ws, void* o_out, void* stream) {
   if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
   if (N <= 0 || R <= 0 || R * N >= (int64_t(1) << 31) || H != 4 || (D != 32 && D != 16)) return TOPS_ERR_SHAPE;
-  const void* ptrs[] = {q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out};
+  const void* ptrs[] = {q_ws, k_ws, vt_ws, bias_ws, o_out};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  if (pen_ws != nullptr && !aligned16(pen_ws)) return TOPS_ERR_ALIGN;
   const int n = static_cast<int>(N);
-  return run_attn<3, 1>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
-                        q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out, static_cast<cudaStream_t>(stream));
+  return run_attn<3>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
+                        q_ws, k_ws, vt_ws, pen_ws, bias_ws, o_out, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int tops_triangle_attn_forward(int dtype, int64_t N, int64_t C, int64_t H, int64_t D, const void* x,
                                           int apply_ln, const float* ln_w, const float* ln_b, const void* w_qkvz,
                                           const float* bz, const uint8_t* mask, float scale, float eps, void* xln_ws,
-                                          void* q_ws, void* k_ws, void* vt_ws, void* maskf_ws, void* bias_ws,
+                                          void* q_ws, void* k_ws, void* vt_ws, void* pen_ws, void* bias_ws,
                                           void* o_out, void* stream) {
   int rc = tops_triangle_attn_project(dtype, N, N, C, H, D, x, apply_ln, ln_w, ln_b, w_qkvz, bz, mask, scale, eps,
-                                      xln_ws, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, stream);
+                                      xln_ws, q_ws, k_ws, vt_ws, pen_ws, bias_ws, stream);
   if (rc != TOPS_OK) return rc;
-  return tops_triangle_attn_attend(dtype, N, N, H, D, q_ws, k_ws, vt_ws, maskf_ws, bias_ws, o_out, stream);
+  return tops_triangle_attn_attend(dtype, N, N, H, D, q_ws, k_ws, vt_ws, mask != nullptr ? pen_ws : nullptr, bias_ws,
+                                   o_out, stream);
 }
 
 extern "C" int tops_fused_gate_forward(int dtype, int64_t T_, int64_t C, const void* o, const void* gin,
@@ -289,17 +297,3 @@ extern "C" int tops_fused_gate_residual(int dtype, int64_t T_, int64_t C, const 
   return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream), residual,
                   static_cast<int>(trans_n));
 }
-
-#ifdef TOPS_TRACE
-// Reads (and clears) the attention phase timers: cycles summed over warps for
-// [0] softmax wait on S, [1] S load + f16 convert + bias, [2] max/exp/rescale,
-// [3] PV wait + P store + arrive, [4] issuer wait on K/V and S release,
-// [5] issuer wait on P, [7] producer wait. Built only with -DTOPS_TRACE.
-extern "C" int tops_attn_trace(unsigned long long* out16) {
-  if (cudaMemcpyFromSymbol(out16, tops::g_attn_trace, 16 * sizeof(unsigned long long)) != cudaSuccess)
-    return TOPS_ERR_CUDA;
-  unsigned long long z[16] = {};
-  cudaMemcpyToSymbol(tops::g_attn_trace, z, sizeof(z));
-  return TOPS_OK;
-}
-#endif

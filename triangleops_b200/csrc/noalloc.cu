@@ -1,8 +1,8 @@
 // noalloc.cu — attention with pair bias for callers that cannot allocate device
 // memory.
 //
-// tops_apb_forward needs five caller-provided workspaces (q, k, v^T, key-mask row,
-// fp32 bias logits). Some hosts of this library cannot provide them: a serving
+// tops_apb_forward needs five caller-provided workspaces (q, k, v^T, key-penalty row,
+// f16 bias logits). Some hosts of this library cannot provide them: a serving
 // runtime that owns a fixed device-memory budget and forbids any allocation after
 // start-up, or an embedding framework that hands out only its own input and output
 // buffers (cudaMalloc there would break its accounting, and cudaMalloc/cudaFree
@@ -12,7 +12,7 @@
 //
 // Limits and rules:
 //   * M <= kNoAllocMaxM (512) tokens; larger M returns TOPS_ERR_CAPACITY and launches
-//     nothing. The array is kNoAllocBytes (about 4.6 MB) and every GPU that loads the
+//     nothing. The array is kNoAllocBytes (about 2.5 MB) and every GPU that loads the
 //     library holds it until the process exits.
 //   * The array is shared by every call on a device and keeps the last call's
 //     contents. Each call writes every workspace byte it later reads, so nothing has
@@ -35,8 +35,8 @@ constexpr size_t na_align(size_t b) { return (b + 255) & ~size_t(255); }
 constexpr size_t na_bytes(int m) {
   return 2 * na_align(size_t(kNoAllocH) * m * kNoAllocD * 2)           // q, k
          + na_align(size_t(kNoAllocH) * kNoAllocD * ((m + 7) & ~7) * 2)  // v^T
-         + na_align(size_t((m + 7) & ~7) * 2)                            // key-mask row
-         + na_align(size_t(kNoAllocH) * m * ((m + 7) & ~7) * 4);         // fp32 bias logits
+         + na_align(size_t((m + 7) & ~7) * 2)                            // key-penalty row
+         + na_align(size_t(kNoAllocH) * m * ((m + 7) & ~7) * 2);         // f16 bias logits
 }
 constexpr size_t kNoAllocBytes = na_bytes(kNoAllocMaxM);
 

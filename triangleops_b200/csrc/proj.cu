@@ -10,8 +10,8 @@
 //   K   =  x~ WK            -> K [R][H][Nk][D]  f16
 //                              (Q, K, V^T are f16 whatever the IO dtype: they are LN-scale
 //                              projections, and f16 keeps three more mantissa bits than bf16)
-//   V   = (x~ WV) * m[i,k]  -> Vt[R][H][D][Nkp]  f16 (transposed, masked keys zeroed)
-//   m   = mask[i,k] ? 1 : 0 -> maskf[R][Nkp]     f16 (the PV MMA turns it into the row sum)
+//   V   =  x~ WV            -> Vt[R][H][D][Nkp]  f16 (transposed)
+//   pen = mask[i,k] ? 0 : -inf -> pen[R][Nkp]     f16 key penalty (only when a mask is given)
 //   Bp  = (x~ WZ^T + BZ) * log2(e) -> Bp[H][R][Nkp] f16 (optional) [triangle_attn/kernel.py:36-98]
 //
 // One GEMM per 128-token tile: x~ (128 x C, K-major, SW128) times the resident
@@ -40,7 +40,7 @@ struct ProjArgs {
   int T;        // tokens
   int Nk;       // positions per row
   int R;        // rows (T = R * Nk)
-  int Nkp;      // padded position stride of Vt / maskf / Bp (multiple of 8)
+  int Nkp;      // padded position stride of Vt / pen / Bp (multiple of 8)
   float scale;  // applied to Q
   float eps;
   const float* ln_w;   // [C] fp32 (HAS_LN)
@@ -51,7 +51,7 @@ struct ProjArgs {
   void* q;
   void* k;
   void* vt;
-  void* maskf;
+  void* pen;           // [R][Nkp] f16 (nullptr = not written)
   void* bp;
   int trans;           // 1: token (i, k) is x[k][i] of a square [Nk][Nk] pair array (ending node)
 };
@@ -262,8 +262,7 @@ __global__ void __launch_bounds__(512, 1)
       const long long tok = proj_token(a, tile, row, valid);
       const int ri = valid ? static_cast<int>(tok / a.Nk) : 0;
       const int kpos = valid ? static_cast<int>(tok - static_cast<long long>(ri) * a.Nk) : 0;
-      float mval = 1.0f;
-      if (a.mask != nullptr && valid) mval = a.mask[static_cast<long long>(ri) * a.Nk + kpos] ? 1.0f : 0.0f;
+      const bool masked = a.mask != nullptr && valid && a.mask[static_cast<long long>(ri) * a.Nk + kpos] == 0;
       uint32_t r[32];
 #pragma unroll
       for (int h = ew * (H / 2); h < (ew + 1) * (H / 2); ++h) {
@@ -290,12 +289,12 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
         }
-        // V (transposed, masked keys zeroed)
+        // V (transposed; masked keys keep their values: their softmax weight is exactly 0)
         if (D == 32) tmem_ld32(lane_addr + 2 * C + h * D, r); else tmem_ld16(lane_addr + 2 * C + h * D, r);
         if (valid) {
           __half* dst = static_cast<__half*>(a.vt) + (static_cast<size_t>(ri) * H + h) * D * a.Nkp + kpos;
 #pragma unroll
-          for (int d = 0; d < D; ++d) dst[static_cast<size_t>(d) * a.Nkp] = __float2half_rn(__uint_as_float(r[d]) * mval);
+          for (int d = 0; d < D; ++d) dst[static_cast<size_t>(d) * a.Nkp] = __float2half_rn(__uint_as_float(r[d]));
         }
       }
       if (HAS_BP && ew == 0) {
@@ -306,7 +305,8 @@ __global__ void __launch_bounds__(512, 1)
             static_cast<__half*>(a.bp)[(static_cast<size_t>(h) * a.R + ri) * a.Nkp + kpos] =
                 __float2half_rn((__uint_as_float(r[h]) + bz[h]) * 1.4426950408889634f);
       }
-      if (valid && ew == 0) static_cast<__half*>(a.maskf)[static_cast<size_t>(ri) * a.Nkp + kpos] = __float2half_rn(mval);
+      if (valid && ew == 0 && a.pen != nullptr)
+        static_cast<unsigned short*>(a.pen)[static_cast<size_t>(ri) * a.Nkp + kpos] = masked ? 0xFC00u : 0u;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.bar_acc_empty);

@@ -225,7 +225,6 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
   S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (a.M + 127) / 128;
-  TOPS_TDECL();
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_w, 1);
     for (int s = 0; s < 2; ++s) {
@@ -268,10 +267,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       int it = 0;
       for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
-        TOPS_TCLK(pa);
         if (!mbar_wait(&sm.x_empty[s], ((it >> 1) & 1) ^ 1, abort, 401)) break;
-        TOPS_TCLK(pb);
-        TOPS_TADD(7, pa, pb);
         mbar_expect_tx(&sm.x_full[s], S::TILE);
         for (int ka = 0; ka < KATOMS; ++ka)
           tma_load_2d(sm.x[s] + ka * 16384, &map_x, &sm.x_full[s], ka * 64, static_cast<int>(tile * 128));
@@ -288,17 +284,11 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       int it = 0;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
-        TOPS_TCLK(ma);
         if (!mbar_wait(&sm.x_full[s], (it >> 1) & 1, abort, 403)) break;
-        TOPS_TCLK(mb);
-        TOPS_TADD(4, ma, mb);
         const uint32_t xa = smem_u32(sm.x[s]), wa = smem_u32(sm.w);
         for (int hh = 0; hh < 2; ++hh) {
           const int u = 2 * it + hh, buf = u & 1;
-          TOPS_TCLK(mc);
           if (!mbar_wait(&sm.acc_empty[buf], ((u >> 1) & 1) ^ 1, abort, 404)) { ok = false; break; }
-          TOPS_TCLK(md);
-          TOPS_TADD(5, mc, md);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < C / 16; ++kk) {
@@ -357,10 +347,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
     int it = 0;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
-      TOPS_TCLK(sa);
       if (!mbar_wait(&sm.st_ready[s], (it >> 1) & 1, abort, 407)) break;
-      TOPS_TCLK(sb2);
-      if (lane == 0) TOPS_TADD(2, sa, sb2);
       const float rstd = sm.rstd[s][row];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.st_free[s]);
@@ -374,10 +361,7 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
       const unsigned long long hm2 = f2_pack(hm, hm);
       for (int hh = 0; hh < 2; ++hh) {
         const int u = 2 * it + hh, buf = u & 1;
-        TOPS_TCLK(ea);
         if (!mbar_wait(&sm.acc_full[buf], (u >> 1) & 1, abort, 408)) { ok = false; break; }
-        TOPS_TCLK(eb);
-        if (lane == 0) TOPS_TADD(0, ea, eb);
         tc_fence_after();
         const uint32_t acc = lane_addr + buf * 256;
         // 8-channel steps, each step's TMEM loads issued before the previous step's math
@@ -428,13 +412,10 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
-        TOPS_TCLK(ec);
-        if (lane == 0) TOPS_TADD(1, eb, ec);
       }
     }
     if (lane == 0) bulk_wait0();
   }
-  TOPS_TFLUSH();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tbase, 512);

@@ -10,7 +10,7 @@ inline int64_t io_bytes(int dtype) { return dtype == TOPS_F32 ? 4 : 2; }
 }  // namespace
 
 // triangle attention over R pair rows of an N x N pair tensor (R = N unsharded):
-// bytes[0..5] = xln, q, k, vt, maskf, bias (the bias for the R rows projected here;
+// bytes[0..5] = xln, q, k, vt, pen, bias (the bias for the R rows projected here;
 // tops_triangle_attn_attend takes the full [H][N][Np] bias, i.e. R = N)
 extern "C" int tops_triangle_attn_workspace_bytes(int dtype, int64_t R, int64_t N, int64_t C, int64_t H, int64_t D,
                                                   int64_t* bytes) {
@@ -22,7 +22,7 @@ extern "C" int tops_triangle_attn_workspace_bytes(int dtype, int64_t R, int64_t 
   bytes[1] = R * H * N * D * 2;            // Q  [R][H][N][D] f16
   bytes[2] = R * H * N * D * 2;            // K
   bytes[3] = R * H * D * np * 2;           // V^T [R][H][D][Np] f16
-  bytes[4] = R * np * 2;                   // mask row [R][Np] f16
+  bytes[4] = R * np * 2;                   // key-penalty rows [R][Np] f16 (masked calls only)
   bytes[5] = H * R * np * 2;               // bias [H][R][Np] f16
   return TOPS_OK;
 }
@@ -39,7 +39,7 @@ extern "C" int tops_trimul_workspace_bytes(int dtype, int64_t B, int64_t L, int6
 }
 
 // attention with pair bias over query rows [q0, q0 + Mq) of M tokens (Mq = M unsharded):
-// bytes[0..4] = q, k, vt, maskf, bias
+// bytes[0..4] = q, k, vt, pen, bias
 extern "C" int tops_apb_workspace_bytes(int64_t M, int64_t Mq, int64_t H, int64_t D, int64_t* bytes) {
   if (bytes == nullptr) return TOPS_ERR_ARG;
   if (M <= 0 || Mq <= 0 || Mq > M || H <= 0 || D <= 0) return TOPS_ERR_SHAPE;
@@ -47,7 +47,7 @@ extern "C" int tops_apb_workspace_bytes(int64_t M, int64_t Mq, int64_t H, int64_
   bytes[0] = H * M * D * 2;   // Q [H][M][D] f16 (all M rows: the row window is read from it)
   bytes[1] = H * M * D * 2;   // K
   bytes[2] = H * D * mp * 2;  // V^T [H][D][Mp]
-  bytes[3] = mp * 2;          // mask row [Mp]
-  bytes[4] = H * Mq * mp * 4; // bias [H][Mq][Mp] fp32
+  bytes[3] = mp * 2;          // key-penalty row [Mp] f16 (masked calls only)
+  bytes[4] = H * Mq * mp * 2; // bias [H][Mq][Mp] f16 (log2 units)
   return TOPS_OK;
 }

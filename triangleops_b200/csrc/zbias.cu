@@ -9,7 +9,9 @@
 // eight lanes share one token (16-byte vector loads, 256 contiguous bytes per
 // token), merge their partial statistics with warp-shuffle Welford (Chan's
 // pairwise update for equal counts) and reduce the H dot products in the same
-// shuffle tree. The logits stay fp32, as in the reference.
+// shuffle tree. The logits are stored as f16 in log2 units, the operand format of the
+// attention kernel (the reference adds them in fp32; f16 keeps 11 bits, |error| below
+// 2^-11 of the logit).
 #include "sm100.cuh"
 
 namespace tops {
@@ -22,7 +24,7 @@ struct ZBiasArgs {
   const float* wc;      // [H][Cz] fp32
   const float* sum_w;   // [H]
   const float* b_const; // [H]
-  float* bias;          // [H][M][Mkp] fp32, in log2 units (times log2(e))
+  __half* bias;         // [H][Mq][Mkp] f16, in log2 units (times log2(e))
 };
 
 template <typename T, int CZ, int H>
@@ -114,7 +116,7 @@ __global__ void __launch_bounds__(256) zbias_kernel(const T* __restrict__ z, ZBi
       for (int h = 0; h < H; ++h)
         if (h == sub) bv = fmaf(rstd, dot[h] - mean * sw[h], bc[h]);
       const long long q = tok / a.M, k = tok - q * a.M;
-      a.bias[(static_cast<long long>(sub) * a.Mq + q) * a.Mkp + k] = bv * 1.4426950408889634f;  // log2 units
+      a.bias[(static_cast<long long>(sub) * a.Mq + q) * a.Mkp + k] = __float2half_rn(bv * 1.4426950408889634f);  // log2 units
     }
   }
 }

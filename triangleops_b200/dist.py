@@ -86,12 +86,6 @@ def triangle_attention_rows(X_rows, pre, *, N, mask_rows=None, scale=1.0, eps=1e
     ws = ops.project(X_rows, pre, mask_rows, N, scale, eps)
     bias_full = all_gather_rows(ws["bias"], 1, group)
     O = ops.attend(ws, bias_full, pre)
-    if mask_rows is not None:
-        from .triangle_attn.module import _fix_fully_masked_rows
-
-        H, D = pre["H"], pre["D"]
-        w = pre["W_qkvz"]
-        _fix_fully_masked_rows(O, ws["xln"], w[2 * H * D:3 * H * D].t(), mask_rows, H, D)
     return ops.gate(O, ws, W_proj_g, W_proj_o)
 
 

@@ -51,8 +51,6 @@ def _tri_attn_residual(x, pre, mask, scale, eps, ending):
     m = None if mask is None else (mask.t() if ending else mask)
     ws = project_rows(src, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=N, mask_rows=m, scale=scale, eps=eps)
     O = attend_rows(ws, ws["bias"], H, D)
-    if m is not None:
-        _ta._fix_fully_masked_rows(O, ws["xln"], w[2 * H * D:3 * H * D].t(), m, H, D)
     gate_forward(O, ws["xln"], pre["W_proj_g"], pre["W_proj_o"], out=x, residual=x, trans_n=N if ending else 0)
     return x
 

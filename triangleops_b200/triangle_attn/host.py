@@ -58,7 +58,7 @@ class HostPipeline:
         self.q = torch.empty(n, H, N, D, dtype=f16, device=dev)
         self.k = torch.empty(n, H, N, D, dtype=f16, device=dev)
         self.vt = torch.empty(n, H, D, nkp, dtype=f16, device=dev)
-        self.maskf = torch.empty(n, nkp, dtype=f16, device=dev)
+        self.pen = torch.empty(n, nkp, dtype=f16, device=dev)  # key penalty rows (masked calls)
         self.bias_slab = torch.empty(self.slabs, H, R, nkp, dtype=f16, device=dev)
         self.bias_local = torch.empty(H, n, nkp, dtype=f16, device=dev)
         self.bias = torch.empty(H, N, nkp, dtype=f16, device=dev)
@@ -85,16 +85,12 @@ class HostPipeline:
         self._setup(n, N, C, X_host.dtype, dev)
         if out_host is None:
             out_host = torch.empty(n, N, C, dtype=X_host.dtype).pin_memory()
-        dead = None
         if mask_host is not None:
             mask_host = mask_host.reshape(n, N)
             if mask_host.dtype == torch.bool:
                 mask_host = mask_host.view(torch.uint8)  # same bytes, still pinned
             elif mask_host.dtype != torch.uint8:
                 mask_host = _mask_u8(mask_host, (n, N))
-            # fully masked rows (the reference's -1e9 turns them into a uniform average
-            # over all keys; the kernel drops masked keys): found on the host, no sync
-            dead = (~mask_host.bool().any(dim=1)).nonzero().flatten()
         compute = torch.cuda.current_stream(dev)
         dt = _lib.dtype_code(X_host.dtype)
         R, H, D, nkp = self.R, self.H, self.D, self.nkp
@@ -115,7 +111,7 @@ class HostPipeline:
                       pre["ln_w32"].data_ptr(), pre["ln_b32"].data_ptr(), self.w.data_ptr(), pre["BZ"].data_ptr(),
                       None if mask_host is None else self.m[r0].data_ptr(), self.scale, self.eps,
                       self.xln[r0].data_ptr(), self.q[r0].data_ptr(), self.k[r0].data_ptr(), self.vt[r0].data_ptr(),
-                      self.maskf[r0].data_ptr(), self.bias_slab[i].data_ptr(), st)
+                      None if mask_host is None else self.pen[r0].data_ptr(), self.bias_slab[i].data_ptr(), st)
             self.ev_proj[i].record(compute)
         # the shared bias, [H][N][Np], from the slabs' [H][R][Np] blocks (and the other ranks' rows)
         if world == 1:
@@ -129,14 +125,9 @@ class HostPipeline:
         for i in range(self.slabs):
             r0, r1 = i * R, (i + 1) * R
             _lib.call("tops_triangle_attn_attend", dt, R, N, H, D, self.q[r0].data_ptr(), self.k[r0].data_ptr(),
-                      self.vt[r0].data_ptr(), self.maskf[r0].data_ptr(), self.bias.data_ptr(), self.o[r0].data_ptr(),
+                      self.vt[r0].data_ptr(), None if mask_host is None else self.pen[r0].data_ptr(),
+                      self.bias.data_ptr(), self.o[r0].data_ptr(),
                       st)
-            if dead is not None:
-                rows = dead[(dead >= r0) & (dead < r1)]
-                if rows.numel():
-                    idx = rows.to(dev, non_blocking=True)
-                    mv = (self.xln[idx].float().mean(dim=1) @ self.w[2 * H * D:3 * H * D].t().float())
-                    self.o[idx] = mv.to(self.o.dtype)[:, None, :].expand(-1, N, -1)
             if self.started:
                 compute.wait_event(self.ev_out[i])  # the previous call's copy-out of this slab
             gate_forward(self.o[r0:r1].view(R * N, H * D), self.xln[r0:r1].view(R * N, C), self.Wg, self.Wo,

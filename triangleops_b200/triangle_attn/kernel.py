@@ -40,14 +40,14 @@ def _workspaces(N, C, H, D, dtype, device, Bias_buf=None):
     q = torch.empty(N, H, N, D, dtype=torch.float16, device=device)
     k = torch.empty(N, H, N, D, dtype=torch.float16, device=device)
     vt = torch.empty(N, H, D, nkp, dtype=torch.float16, device=device)
-    maskf = torch.empty(N, nkp, dtype=torch.float16, device=device)
+    pen = torch.empty(N, nkp, dtype=torch.float16, device=device)  # key penalty (0 / -inf), masked calls
     # the shared bias is kept in f16, pre-scaled by log2(e) (the attention kernel works in log2 units)
     if Bias_buf is not None and nkp == N and Bias_buf.is_contiguous() and Bias_buf.shape == (H, N, N) \
             and Bias_buf.dtype == torch.float16:
         bias = Bias_buf
     else:
         bias = torch.empty(H, N, nkp, dtype=torch.float16, device=device)
-    return q, k, vt, maskf, bias
+    return q, k, vt, pen, bias
 
 
 def triangle_attn_fused_forward(X, w_qkvz, ln_w, ln_b, bz, H, D, *, mask=None, scale=1.0, eps=1e-5, out=None,
@@ -62,11 +62,11 @@ def triangle_attn_fused_forward(X, w_qkvz, ln_w, ln_b, bz, H, D, *, mask=None, s
         out = torch.empty(N, N, H * D, dtype=X.dtype, device=X.device)
     if xln_out is None:
         xln_out = torch.empty(N, N, C, dtype=X.dtype, device=X.device)
-    q, k, vt, maskf, bias = _workspaces(N, C, H, D, X.dtype, X.device)
+    q, k, vt, pen, bias = _workspaces(N, C, H, D, X.dtype, X.device)
     m = _mask_u8(mask, (N, N))
     _lib.call("tops_triangle_attn_forward", dt, N, C, H, D, X.data_ptr(), 1, ln_w.data_ptr(), ln_b.data_ptr(),
               w_qkvz.data_ptr(), bz.data_ptr(), _lib.ptr(m), float(scale), float(eps), xln_out.data_ptr(),
-              q.data_ptr(), k.data_ptr(), vt.data_ptr(), maskf.data_ptr(), bias.data_ptr(), out.data_ptr(),
+              q.data_ptr(), k.data_ptr(), vt.data_ptr(), pen.data_ptr(), bias.data_ptr(), out.data_ptr(),
               _lib.stream_ptr(X.device))
     return out, xln_out
 
@@ -88,11 +88,11 @@ def triangle_attn_forward(X_ln, WQ_c, WKV_c, WZ_c, BZ, out, scale=1.0, mask=None
     bz = BZ.float().contiguous()
     X_ln = X_ln.contiguous()
     dst = out if out.is_contiguous() else torch.empty(N, N, H * D, dtype=X_ln.dtype, device=X_ln.device)
-    q, k, vt, maskf, bias = _workspaces(N, C, H, D, X_ln.dtype, X_ln.device, Bias_buf)
+    q, k, vt, pen, bias = _workspaces(N, C, H, D, X_ln.dtype, X_ln.device, Bias_buf)
     m = _mask_u8(mask, (N, N))
     _lib.call("tops_triangle_attn_forward", dt, N, C, H, D, X_ln.data_ptr(), 0, None, None, w.data_ptr(),
               bz.data_ptr(), _lib.ptr(m), float(scale), 1e-5, None, q.data_ptr(), k.data_ptr(), vt.data_ptr(),
-              maskf.data_ptr(), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(X_ln.device))
+              pen.data_ptr(), bias.data_ptr(), dst.data_ptr(), _lib.stream_ptr(X_ln.device))
     if dst is not out:
         out.copy_(dst)
     return out
@@ -157,9 +157,9 @@ def is_transposed_rows(X_rows):
 def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, scale=1.0, eps=1e-5):
     """LN + Q/K/V/bias projection of R pair rows X_rows (R, N, C).
 
-    Returns dict(q, k, vt, maskf, bias, xln): bias holds this slab's rows of the
+    Returns dict(q, k, vt, pen, bias, xln): bias holds this slab's rows of the
     shared bias, (H, R, Np) f16 in log2 units; the others are row-local attention
-    operands (vt and maskf f16). X_rows may be rows of a transposed view
+    operands (vt f16; pen, the f16 key penalty 0 / -inf, or None without a mask). X_rows may be rows of a transposed view
     (``X.transpose(0, 1)[r0:r1]`` of a contiguous square X, the ending node): the
     projection then reads X column-wise through a 3-D tensor map, without a copy."""
     _lib.require_cuda(X_rows)
@@ -176,14 +176,14 @@ def project_rows(X_rows, w_qkvz, ln_w, ln_b, bz, H, D, *, N, mask_rows=None, sca
     ws = dict(q=torch.empty(R, H, N, D, dtype=torch.float16, device=dev),
               k=torch.empty(R, H, N, D, dtype=torch.float16, device=dev),
               vt=torch.empty(R, H, D, nkp, dtype=torch.float16, device=dev),
-              maskf=torch.empty(R, nkp, dtype=torch.float16, device=dev),
+              pen=None if mask_rows is None else torch.empty(R, nkp, dtype=torch.float16, device=dev),
               bias=torch.empty(H, R, nkp, dtype=torch.float16, device=dev),
               xln=torch.empty(R, N, C, dtype=dty, device=dev))
     m = _mask_u8(mask_rows, (R, N))
     _lib.call(entry, dt, R, N, C, H, D, X_rows.data_ptr(), 1, ln_w.data_ptr(),
               ln_b.data_ptr(), w_qkvz.data_ptr(), bz.data_ptr(), _lib.ptr(m), float(scale), float(eps),
               ws["xln"].data_ptr(), ws["q"].data_ptr(), ws["k"].data_ptr(), ws["vt"].data_ptr(),
-              ws["maskf"].data_ptr(), ws["bias"].data_ptr(), _lib.stream_ptr(dev))
+              _lib.ptr(ws["pen"]), ws["bias"].data_ptr(), _lib.stream_ptr(dev))
     return ws
 
 
@@ -196,6 +196,6 @@ def attend_rows(ws, bias_full, H, D, out=None):
     if out is None:
         out = torch.empty(R, N, H * D, dtype=io, device=ws["q"].device)
     _lib.call("tops_triangle_attn_attend", dt, R, N, H, D, ws["q"].data_ptr(), ws["k"].data_ptr(),
-              ws["vt"].data_ptr(), ws["maskf"].data_ptr(), bias_full.data_ptr(), out.data_ptr(),
+              ws["vt"].data_ptr(), _lib.ptr(ws["pen"]), bias_full.data_ptr(), out.data_ptr(),
               _lib.stream_ptr(out.device))
     return out

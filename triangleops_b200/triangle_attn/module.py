@@ -48,19 +48,6 @@ def precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D):
     }
 
 
-def _fix_fully_masked_rows(O, X_ln, WV, mask, H, D):
-    """Rows whose key mask is all False: the reference's additive -1e9 makes every
-    score equal in fp32, i.e. a uniform average of V over all N keys
-    (``triangle_attn/kernel.py:233-238``). The B200 kernel drops masked keys exactly,
-    so such rows are patched here with mean_k V[i, k] = (mean_k x~[i, k]) W_V."""
-    dead = ~mask.reshape(mask.shape[0], -1).to(torch.bool).any(dim=1)
-    if bool(dead.any()):
-        idx = dead.nonzero().flatten()
-        mv = (X_ln[idx].float().mean(dim=1) @ WV.float()).to(O.dtype)  # (n_dead, H*D)
-        O[idx] = mv[:, None, :].expand(-1, O.shape[1], -1)
-    return O
-
-
 def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_proj_o, B_proj_o, pad_to=32):
     """Per-call forward (``module.py:53-121``). X is (N, N, C); returns (N, N, C).
     ``pad_to`` is accepted for signature compatibility; the TMA-fed kernels handle
@@ -83,9 +70,6 @@ def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_pro
     else:
         O, X_ln = triangle_attn_fused_forward(X, w, pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, mask=mask,
                                               scale=scale, eps=eps)
-    if mask is not None:
-        WV = w[2 * H * D:3 * H * D].t()
-        _fix_fully_masked_rows(O, X_ln, WV, mask, H, D)
     return gate_forward(O, X_ln, W_proj_g, W_proj_o).view(N, N, -1)
 
 
