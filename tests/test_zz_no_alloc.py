@@ -5,7 +5,8 @@ or embedding framework that owns a fixed device-memory budget and forbids any
 allocation once it is running. ``tops_apb_forward_noalloc`` serves them by
 keeping its workspaces in a library-owned static device array (M <= 512). This
 test calls it through the C ABI, twice in a row with different inputs, and
-compares each result with the regular ``tops_apb_forward`` on the same inputs.
+checks that each result is bit-identical to the regular ``tops_apb_forward`` on the
+same inputs.
 The file name sorts last so a stop-at-first-failure run has run everything else.
 """
 import ctypes
@@ -13,7 +14,6 @@ import ctypes
 import pytest
 import torch
 
-from helpers import RTOL, TOL
 from triangleops_b200 import _lib
 from triangleops_b200.attn_pair_bias.kernel import apb_core
 from triangleops_b200._common.layouts import qkv_rows
@@ -58,10 +58,11 @@ def test_noalloc_matches_regular_entry_point_twice(device):
         apb_core(X, w, Z, Wc, sW, Bc, ref, 4, 32, scale=scale, key_mask=km)
         torch.cuda.synchronize()
         assert _lib.device_error()[0] == 0
-        g, r = got.double(), ref.double()
-        assert torch.isfinite(g).all()
-        excess = ((g - r).abs() - (TOL[torch.bfloat16] + RTOL[torch.bfloat16] * r.abs())).max().item()
-        assert excess <= 0, f"M={M}: noalloc differs from tops_apb_forward by {excess:.3e} over the bar"
+        assert torch.isfinite(got).all()
+        # the same kernels with the same launch shapes run on the same inputs: any
+        # difference would come from the static scratch carve-up, so the bar is bit-equality
+        assert torch.equal(got, ref), f"M={M}: noalloc differs from tops_apb_forward " \
+            f"(max |d| {(got.double() - ref.double()).abs().max().item():.3e})"
 
 
 def test_noalloc_rejects_oversize(device):

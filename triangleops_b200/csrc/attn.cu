@@ -13,22 +13,28 @@
 // rows ("tiles", 128 queries each) of the same head and query block: each bias tile
 // read from L2 serves TR rows.
 //
-// Cost model (measured on B200): one thread issues at most one tcgen05.mma per ~113
-// cycles whatever N is, and MMAs of several threads overlap; an MMA reading A from
-// TMEM (TS) with N=64 runs near the tensor peak once three threads issue, while an
-// SS MMA with N=64 is capped near 60% of it by its shared-memory reads. Each tile
-// therefore has its own QK^T issuer and PV issuer (6 MMA streams for TR=3), the PV
-// MMA takes P from TMEM, and the bias is not added by the tensor core: the tile-0
-// issuer copies the block's f16 bias tile from shared memory into TMEM once
-// (tcgen05.cp, 4 x 128x256b), and every softmax warpgroup loads its rows from there
-// and adds them to S in registers (one f16x2 add per key pair).
+// The tensor core builds S completely, so the softmax does per element only the max,
+// the subtraction and 2^x. Per 64-key block and tile, one thread issues into the f16
+// accumulator S:
+//   S  = bias x I          4 MMAs (K = 64 keys in steps of 16; I = 64 x 64 identity)
+//   S += Q K^T             D/16 MMAs
+//   S += 1 x pen           1 MMA, masked calls only: A is a 128 x 16 tile of ones and
+//                          B an MN-major 16 x 64 tile whose row 0 is the pair row's
+//                          penalty row (rows 1..15 zero), so every query gets pen[k]
+// and one thread issues PV: O += P V^T (P from TMEM, 4 MMAs of 16 keys).
 //
-// Per CTA: w0 TMA producer (per 64-key block: bias and K tiles into ring A; V^T
-// tiles and penalty rows into ring B), w(1+t) QK^T issuer of tile t (t = 0 also
-// copies the bias into TMEM), w(1+TR+t) PV issuer of tile t, one softmax warpgroup
-// per tile (one TMEM lane = one query row per thread). TMEM per tile: S (64 f16
-// columns), P (32 columns of packed f16 pairs, the A operand of PV), O (D+16 fp32
-// columns: D values, the row sum, zero padding); plus two bias stages of 32 columns.
+// Cost model (measured on B200): a warp pays ~82 cycles to issue one SS tcgen05.mma
+// and ~164 cycles for a TS one (A from TMEM), whatever N is, and MMAs of different
+// warps overlap. The f16 pair pipe (add/sub/fma on f16x2) and the MUFU are what the
+// softmax spends its time on, so every per-element add that the tensor core can do
+// instead is moved there.
+//
+// Per CTA: w0 TMA producer A (per 64-key block: bias, TR K tiles and TR penalty rows
+// into ring A; the unit's Q tiles), w1 TMA producer B (TR V^T tiles into ring B),
+// w(2+t) S issuer of tile t, w(2+TR+t) PV issuer of tile t, one softmax warpgroup per
+// tile (one TMEM lane = one query row per thread). TMEM per tile: S (64 f16 columns),
+// P (32 columns of packed f16 pairs per buffer, the A operand of PV; two buffers when
+// TMEM has room), O (D+16 fp32 columns: D values, the row sum, zero padding).
 //
 // Row sum without per-element work: row D of every V^T operand tile is 1.0 (written
 // once), so the PV MMA also produces l = sum_k p_k in accumulator column D.
@@ -36,13 +42,12 @@
 // Online softmax in the exp2 domain (Q carries scale*log2(e) and the bias log2(e),
 // both folded in upstream) with lazy rescaling (O is only rescaled when the running
 // max grows by more than 2^8). The per-element work runs on f16 pairs: the tensor
-// core accumulates S = Q K^T in f16 (each of the D/16 steps rounds once, relative
-// error 2^-11, below the 2^-8 rounding the 16-bit Q and K already put into S), the
-// softmax loads it as packed pairs (tcgen05.ld .pack::16b), adds bias and penalty,
-// takes the row max as a pairwise tree, and computes P = 2^(x - m) with 2/3 of the
-// pairs on the MUFU (ex2.approx.f16x2, two XU issues per pair) and 1/3 by a
-// polynomial on the FMA pipe (ex2_poly_f16x2), so that neither pipe alone bounds
-// the step.
+// core accumulates S in f16 (each step rounds once, relative error 2^-11, below the
+// 2^-8 rounding the 16-bit operands already put into S), the softmax loads it as
+// packed pairs (tcgen05.ld .pack::16b), takes the row max as a pairwise tree, and
+// computes P = 2^(x - m) with part of the pairs on the MUFU (ex2.approx.f16x2) and
+// the rest by a polynomial on the FMA pipe (ex2_poly_f16x2), so that neither pipe
+// alone bounds the step.
 #include "sm100.cuh"
 
 namespace tops {
@@ -54,9 +59,10 @@ namespace tops {
 template <int D, int TR>
 struct AttnCfg {
   static constexpr int NT = TR;                 // tiles (128 queries x 1 row) per CTA
-  // warps: 0 TMA producer, 1..NT QK^T issuers, NT+1..2NT PV issuers, then one softmax
-  // warpgroup per tile (any 4 consecutive warps cover the 4 TMEM lane quarters)
-  static constexpr int SM_WARP0 = 1 + 2 * NT;
+  // warps: 0 and 1 TMA producers (ring A, ring B), 2..NT+1 S issuers, NT+2..2NT+1 PV
+  // issuers, then one softmax warpgroup per tile (any 4 consecutive warps cover the 4
+  // TMEM lane quarters)
+  static constexpr int SM_WARP0 = 2 + 2 * NT;
   static constexpr int THREADS = 32 * SM_WARP0 + 128 * NT;
   static constexpr int BK = 64;                 // keys per block
   static constexpr int NPV = D + 16;            // PV N: D value columns + ones row + zero pad
@@ -64,24 +70,28 @@ struct AttnCfg {
   static constexpr int K_BYTES = BK * D * 2;
   static constexpr int V_BYTES = NPV * 128;     // NPV rows x 64 keys (128 B, SW128)
   static constexpr int BIAS_BYTES = 128 * BK * 2;  // f16 bias tile [128 q][64 k], SW128
-  // ring A: the bias tile and the TR K tiles (free once the bias copy and every QK^T
-  // of the block have run); ring B: the TR V^T tiles and TR penalty rows (free once
-  // every PV of the block has run, which follows the softmax's penalty read)
-  static constexpr int A_BYTES = BIAS_BYTES + TR * K_BYTES;
-  static constexpr int PEN_OFF = TR * V_BYTES;
-  static constexpr int B_BYTES = (PEN_OFF + TR * 128 + 1023) / 1024 * 1024;
+  static constexpr int PEN_BYTES = 16 * 128;    // MN-major 16 x 64 tile, row 0 = penalty row
+  // ring A: the bias tile, the TR K tiles and the TR penalty tiles (free once every S
+  // MMA of the block has run); ring B: the TR V^T tiles (free once every PV has run)
+  static constexpr int K_OFF = BIAS_BYTES;
+  static constexpr int PEN_OFF = BIAS_BYTES + TR * K_BYTES;
+  static constexpr int A_BYTES = PEN_OFF + TR * PEN_BYTES;
+  static constexpr int B_BYTES = TR * V_BYTES;
   static constexpr int NA = 3;
-  static constexpr int NB = 4;
+  static constexpr int NB = 3;
   static constexpr uint32_t QK_SW = D == 32 ? kSw64 : kSw32;
   static constexpr int QK_SBO = 8 * D * 2;       // 8 rows x row bytes
-  static constexpr int S_COL = 0;                // S of tile t at t*64
-  static constexpr int P_COL = 64 * NT;          // P of tile t at P_COL + t*32
-  static constexpr int O_COL = P_COL + 32 * NT;  // O of tile t at O_COL + t*NPV
-  static constexpr int BIAS_COL = O_COL + NPV * NT;  // bias stage b at BIAS_COL + b*32
-  static constexpr int TMEM_USED = BIAS_COL + 64;
+  // P buffers per tile: two when TMEM has room (the softmax then writes P(j+1) while
+  // PV(j) still reads P(j)), else one
+  static constexpr int NPB = (64 + 64 + NPV) * NT <= 512 ? 2 : 1;
+  static constexpr int S_COL = 0;                      // S of tile t at t*64
+  static constexpr int P_COL = 64 * NT;                // P buffer b of tile t at P_COL + (t*NPB + b)*32
+  static constexpr int O_COL = P_COL + 32 * NPB * NT;  // O of tile t at O_COL + t*NPV
+  static constexpr int TMEM_USED = O_COL + NPV * NT;
   static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
-  static_assert(A_BYTES % 1024 == 0 && V_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "alignment");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0 && PEN_OFF % 1024 == 0,
+                "alignment");
 };
 
 struct AttnArgs {
@@ -97,48 +107,26 @@ struct AttnSmem {
   alignas(1024) uint8_t q[Cfg::NT][Cfg::Q_BYTES];
   alignas(1024) uint8_t ring_a[Cfg::NA][Cfg::A_BYTES];
   alignas(1024) uint8_t ring_b[Cfg::NB][Cfg::B_BYTES];
+  alignas(1024) uint8_t ident[64 * 128];   // f16 identity (64 x 64, K-major SW128)
+  alignas(1024) uint8_t ones[128 * 32];    // f16 ones (128 x 16, K-major)
   uint64_t bar_q;
-  uint64_t q_empty;            // one commit per tile issuer (after the unit's last QK^T)
+  uint64_t q_empty;            // one commit per S issuer (after the unit's last QK^T)
   uint64_t a_full[Cfg::NA];
-  uint64_t a_empty[Cfg::NA];   // one commit per tile issuer (tile 0's also covers the bias copy)
+  uint64_t a_empty[Cfg::NA];   // one commit per S issuer
   uint64_t b_full[Cfg::NB];
-  uint64_t b_empty[Cfg::NB];   // one commit per tile issuer (after PV)
-  uint64_t bias_full[2];       // the block's bias tile copied into TMEM stage gg&1
-  uint64_t bias_empty[2];      // every softmax warp has loaded it
-  uint64_t s_full[Cfg::NT];    // QK^T of the block landed in S
+  uint64_t b_empty[Cfg::NB];   // one commit per PV issuer
+  uint64_t s_full[Cfg::NT];    // S of the block complete
   uint64_t s_free[Cfg::NT];    // the softmax has loaded S (it may be overwritten)
   uint64_t p_full[Cfg::NT];    // P of the block written
-  uint64_t pv_done[Cfg::NT];   // PV of the block finished (P reusable, O stable)
+  uint64_t pv_done[Cfg::NT][2];  // PV of a block using P buffer b finished (P reusable, O stable)
   uint64_t o_full[Cfg::NT];    // the last PV of the unit finished
   uint64_t o_empty[Cfg::NT];   // the epilogue has read O (the next unit may overwrite it)
   uint32_t tmem_base;
   int abort;
 };
 
-// smem (tcgen05 matrix descriptor) -> TMEM copy of 128 rows x 256 bits; with the
-// SW128 K-major descriptor of a 16-column slice of a 16-bit tile, TMEM column c of
-// lane m receives elements (m, 2c) | (m, 2c+1) << 16 (measured on B200).
-__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t desc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
-}
-
-// Half of S (32 columns of f16 accumulators, packed pairwise into 16 registers) and
-// the matching half of the bias stage (16 columns of packed pairs) in one round trip.
-__device__ __forceinline__ void tmem_ld_s_bias_half(uint32_t s_addr, uint32_t b_addr, uint32_t* s, uint32_t* b) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.pack::16b.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(s[0]), "=r"(s[1]), "=r"(s[2]), "=r"(s[3]), "=r"(s[4]), "=r"(s[5]), "=r"(s[6]), "=r"(s[7]), "=r"(s[8]), "=r"(s[9]), "=r"(s[10]), "=r"(s[11]), "=r"(s[12]), "=r"(s[13]), "=r"(s[14]), "=r"(s[15]),
-        "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])
-      : "r"(s_addr), "r"(b_addr) : "memory");
-}
-
-__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
+__device__ __forceinline__ float f16lo(uint32_t p) { return __half2float(__ushort_as_half(static_cast<unsigned short>(p & 0xFFFFu))); }
+__device__ __forceinline__ float f16hi(uint32_t p) { return __half2float(__ushort_as_half(static_cast<unsigned short>(p >> 16))); }
 __device__ __forceinline__ uint32_t hmax2_u(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -149,8 +137,6 @@ __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-__device__ __forceinline__ float f16lo(uint32_t p) { return __half2float(__ushort_as_half(static_cast<unsigned short>(p & 0xFFFFu))); }
-__device__ __forceinline__ float f16hi(uint32_t p) { return __half2float(__ushort_as_half(static_cast<unsigned short>(p >> 16))); }
 
 constexpr uint32_t kF16NegInf2 = 0xFC00FC00u;
 
@@ -161,24 +147,37 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
                 const __grid_constant__ CUtensorMap map_b, AttnArgs a) {
   using Cfg = AttnCfg<D, TR>;
   using E = Elem<T>;
-  constexpr int NA = Cfg::NA, NB = Cfg::NB, NT = Cfg::NT, BK = Cfg::BK;
+  constexpr int NA = Cfg::NA, NB = Cfg::NB, NT = Cfg::NT, BK = Cfg::BK, NPB = Cfg::NPB;
   extern __shared__ uint8_t smem_raw[];
   auto& sm = *reinterpret_cast<AttnSmem<D, TR>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (a.Nk + BK - 1) / BK;
   const int H = a.H;
   const bool has_mask = a.has_mask != 0;
-  auto k_tile = [&](int s, int r) { return sm.ring_a[s] + Cfg::BIAS_BYTES + r * Cfg::K_BYTES; };
+  auto k_tile = [&](int s, int r) { return sm.ring_a[s] + Cfg::K_OFF + r * Cfg::K_BYTES; };
+  auto pen_tile = [&](int s, int r) { return sm.ring_a[s] + Cfg::PEN_OFF + r * Cfg::PEN_BYTES; };
   auto v_tile = [&](int s, int r) { return sm.ring_b[s] + r * Cfg::V_BYTES; };
 
-  // rows D .. NPV-1 of every V^T operand tile: row D all ones (the row-sum column of
-  // PV), the rest zero; written once (TMA fills rows 0 .. D-1 only). 32 words per row.
+  // Constant operand parts, written once (TMA never touches them):
+  //  * rows D .. NPV-1 of every V^T tile: row D all ones (the row-sum column of PV), the rest zero;
+  //  * rows 1..15 of every penalty tile (TMA fills row 0 only);
+  //  * the 64 x 64 identity (element (n, k) at n*128 + ((k/8 ^ n%8) * 16) + (k%8)*2) and the ones tile.
   constexpr int EXTRA_ROWS = Cfg::NPV - D;
   for (int idx = threadIdx.x; idx < NB * NT * EXTRA_ROWS * 32; idx += blockDim.x) {
     const int w = idx & 31, rowp = (idx >> 5) % EXTRA_ROWS, rs = idx / (EXTRA_ROWS * 32);
     uint32_t* v = reinterpret_cast<uint32_t*>(v_tile(rs / NT, rs % NT));
     v[(D + rowp) * 32 + w] = rowp == 0 ? 0x3C003C00u : 0u;
   }
+  for (int idx = threadIdx.x; idx < NA * NT * 15 * 32; idx += blockDim.x) {
+    const int w = idx & 31, rowp = (idx >> 5) % 15, rs = idx / (15 * 32);
+    reinterpret_cast<uint32_t*>(pen_tile(rs / NT, rs % NT))[(1 + rowp) * 32 + w] = 0u;
+  }
+  for (int w = threadIdx.x; w < 64 * 32; w += blockDim.x) {
+    const int n = w >> 5, pc = w & 31;          // row n, 32-bit word pc of the 128-byte row
+    const int k0 = ((pc >> 2) ^ (n & 7)) * 8 + (pc & 3) * 2;  // logical column of the word's low half
+    reinterpret_cast<uint32_t*>(sm.ident)[w] = (k0 == n ? 0x3C00u : 0u) | (k0 + 1 == n ? 0x3C000000u : 0u);
+  }
+  for (int w = threadIdx.x; w < 128 * 8; w += blockDim.x) reinterpret_cast<uint32_t*>(sm.ones)[w] = 0x3C003C00u;
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_q, 1);
     mbar_init(&sm.q_empty, NT);
@@ -190,15 +189,12 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       mbar_init(&sm.b_full[s], 1);
       mbar_init(&sm.b_empty[s], NT);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.bias_full[b], 1);
-      mbar_init(&sm.bias_empty[b], 4 * NT);
-    }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.s_free[t], 4);
       mbar_init(&sm.p_full[t], 4);
-      mbar_init(&sm.pv_done[t], 1);
+      mbar_init(&sm.pv_done[t][0], 1);
+      mbar_init(&sm.pv_done[t][1], 1);
       mbar_init(&sm.o_full[t], 1);
       mbar_init(&sm.o_empty[t], 4);
     }
@@ -217,7 +213,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
   // 128-query block of one head (query block fastest: the CTAs running together share
   // the bias tiles of a head and the K/V of a row in L2). Ring slots and barrier
   // phases run on across units (g = blocks processed by this CTA so far, lu = units
-  // so far), so the producer streams the next unit's tiles while the current one ends.
+  // so far), so the producers stream the next unit's tiles while the current one ends.
   const int n_qb = (a.Nq + 127) / 128;
   const int n_rg = (a.R + TR - 1) / TR;
   const int n_units = n_qb * n_rg * a.H;
@@ -229,47 +225,66 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
   };
 
   if (warp == 0) {
+    // ---------------- TMA producer A: bias, K and penalty tiles (ring A), Q tiles ----------------
+    // The whole warp runs the loop; lane r issues the load of tile r, so the loads of a
+    // block go out as few warp instructions.
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
-      tma_prefetch_desc(&map_v);
       tma_prefetch_desc(&map_b);
       if (has_mask) tma_prefetch_desc(&map_pen);
-      const uint32_t b_tx = NT * (D * 128) + (has_mask ? NT * 128 : 0);
-      bool ok = true;
-      int g = 0, lu = 0;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
-        int q0, row0, h;
-        coords(u, q0, row0, h);
-        for (int j = 0; j < nkb; ++j) {
-          const int gg = g + j, s = gg % NA, sb = gg % NB, k0 = j * BK;
-          if (!mbar_wait(&sm.a_empty[s], ((gg / NA) & 1) ^ 1, abort, 201)) { ok = false; break; }
-          mbar_expect_tx(&sm.a_full[s], Cfg::A_BYTES);
-          tma_load_3d(sm.ring_a[s], &map_b, &sm.a_full[s], k0, q0, h);
-          for (int r = 0; r < NT; ++r) tma_load_3d(k_tile(s, r), &map_k, &sm.a_full[s], 0, k0, (row0 + r) * H + h);
-          if (j == 0) {
-            // the unit's Q tiles, once the previous unit's last QK^T has read them
-            if (!mbar_wait(&sm.q_empty, (lu & 1) ^ 1, abort, 213)) { ok = false; break; }
-            mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
-            for (int t = 0; t < NT; ++t) tma_load_3d(sm.q[t], &map_q, &sm.bar_q, 0, q0, (row0 + t) * H + h);
-          }
-          if (!mbar_wait(&sm.b_empty[sb], ((gg / NB) & 1) ^ 1, abort, 211)) { ok = false; break; }
-          mbar_expect_tx(&sm.b_full[sb], b_tx);
-          for (int r = 0; r < NT; ++r) {
-            tma_load_3d(v_tile(sb, r), &map_v, &sm.b_full[sb], k0, 0, (row0 + r) * H + h);
-            if (has_mask) tma_load_2d(sm.ring_b[sb] + Cfg::PEN_OFF + r * 128, &map_pen, &sm.b_full[sb], k0, row0 + r);
-          }
+    }
+    const uint32_t a_tx = Cfg::BIAS_BYTES + NT * Cfg::K_BYTES + (has_mask ? NT * 128 : 0);
+    bool ok = true;
+    int g = 0, lu = 0;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+      int q0, row0, h;
+      coords(u, q0, row0, h);
+      for (int j = 0; j < nkb; ++j) {
+        const int gg = g + j, s = gg % NA, k0 = j * BK;
+        if (!mbar_wait(&sm.a_empty[s], ((gg / NA) & 1) ^ 1, abort, 201)) { ok = false; break; }
+        if (lane == 0) mbar_expect_tx(&sm.a_full[s], a_tx);
+        __syncwarp();
+        if (lane == NT) tma_load_3d(sm.ring_a[s], &map_b, &sm.a_full[s], k0, q0, h);
+        else if (lane < NT) tma_load_3d(k_tile(s, lane), &map_k, &sm.a_full[s], 0, k0, (row0 + lane) * H + h);
+        else if (has_mask && lane >= 16 && lane < 16 + NT)
+          tma_load_2d(pen_tile(s, lane - 16), &map_pen, &sm.a_full[s], k0, row0 + lane - 16);
+        if (j == 0) {
+          // the unit's Q tiles, once the previous unit's last QK^T has read them
+          if (!mbar_wait(&sm.q_empty, (lu & 1) ^ 1, abort, 213)) { ok = false; break; }
+          if (lane == 0) mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
+          __syncwarp();
+          if (lane < NT) tma_load_3d(sm.q[lane], &map_q, &sm.bar_q, 0, q0, (row0 + lane) * H + h);
         }
       }
     }
-  } else if (warp <= NT) {
+  } else if (warp == 1) {
+    // ---------------- TMA producer B: V^T tiles (ring B) ----------------
+    if (lane == 0) tma_prefetch_desc(&map_v);
+    const uint32_t b_tx = NT * (D * 128);
+    bool ok = true;
+    int g = 0;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, g += nkb) {
+      int q0, row0, h;
+      coords(u, q0, row0, h);
+      (void)q0;
+      for (int j = 0; j < nkb; ++j) {
+        const int gg = g + j, sb = gg % NB, k0 = j * BK;
+        if (!mbar_wait(&sm.b_empty[sb], ((gg / NB) & 1) ^ 1, abort, 211)) { ok = false; break; }
+        if (lane == 0) mbar_expect_tx(&sm.b_full[sb], b_tx);
+        __syncwarp();
+        if (lane < NT) tma_load_3d(v_tile(sb, lane), &map_v, &sm.b_full[sb], k0, 0, (row0 + lane) * H + h);
+      }
+    }
+  } else if (warp <= NT + 1) {
     if (lane == 0) {
-      // ---------------- QK^T issuer of tile t (tile 0 also copies the bias) ----------------
-      const int t = warp - 1;
-      // Q, K are f16; S is accumulated in f16 (D format 0)
-      const uint32_t idesc_qk = make_idesc_f16(128, BK, 0, false, false) & ~(3u << 4);
-      const uint32_t qa = smem_u32(sm.q[t]);
+      // ---------------- S issuer of tile t: bias x I, Q K^T, 1 x pen ----------------
+      const int t = warp - 2;
+      // every S operand is f16; S is accumulated in f16 (D format 0)
+      const uint32_t idesc_s = make_idesc_f16(128, BK, 0, false, false) & ~(3u << 4);
+      const uint32_t idesc_pen = make_idesc_f16(128, BK, 0, false, true) & ~(3u << 4);
+      const uint32_t qa = smem_u32(sm.q[t]), ia = smem_u32(sm.ident);
+      const uint64_t ones_desc = make_smem_desc(smem_u32(sm.ones), 16, 256, kSw32);
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       bool ok = true;
       int g = 0, lu = 0;
@@ -278,36 +293,32 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
         for (int j = 0; j < nkb; ++j) {
           const int gg = g + j, s = gg % NA;
           if (!mbar_wait(&sm.a_full[s], (gg / NA) & 1, abort, 203)) { ok = false; break; }
-          if (t == 0) {
-            // bias tile -> TMEM stage gg&1, once every softmax warp has loaded block gg-2 from it
-            if (!mbar_wait(&sm.bias_empty[gg & 1], ((gg >> 1) & 1) ^ 1, abort, 215)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t ba = smem_u32(sm.ring_a[s]);
-            const uint32_t bt = tbase + Cfg::BIAS_COL + (gg & 1) * 32;
-#pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) tmem_cp_128x256b(bt + kk * 8, make_smem_desc(ba + kk * 32, 16, 1024, kSw128));
-            mma_commit(&sm.bias_full[gg & 1]);
-          }
           if (gg > 0 && !mbar_wait(&sm.s_free[t], (gg - 1) & 1, abort, 204)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t ka = smem_u32(k_tile(s, t));
+          const uint32_t ba = smem_u32(sm.ring_a[s]), ka = smem_u32(k_tile(s, t));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_ss(s_tmem, make_smem_desc(ba + kk * 32, 16, 1024, kSw128), make_smem_desc(ia + kk * 32, 16, 1024, kSw128),
+                   idesc_s, kk > 0);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
-                   make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_qk, kk > 0);
+                   make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_s, 1);
+          if (has_mask)
+            mma_ss(s_tmem, ones_desc, make_smem_desc(smem_u32(pen_tile(s, t)), 2048, 1024, kSw128), idesc_pen, 1);
           mma_commit(&sm.s_full[t]);
-          mma_commit(&sm.a_empty[s]);  // K (and, tile 0, the bias tile) consumed once these finish
+          mma_commit(&sm.a_empty[s]);  // bias, K and penalty tiles consumed once these finish
           if (j == nkb - 1) mma_commit(&sm.q_empty);  // Q of this unit no longer needed
         }
       }
     }
-  } else if (warp <= 2 * NT) {
+  } else if (warp <= 2 * NT + 1) {
     if (lane == 0) {
       // ---------------- PV issuer of tile t ----------------
-      const int t = warp - 1 - NT;
+      const int t = warp - 2 - NT;
       // P (ex2 output) and V^T are f16 whatever the IO dtype.
       const uint32_t idesc_pv = make_idesc_f16(128, Cfg::NPV, 0, false, false);
-      const uint32_t p_tmem = tbase + Cfg::P_COL + t * 32;
+      const uint32_t p_tmem0 = tbase + Cfg::P_COL + t * 32 * NPB;
       const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
       bool ok = true;
       int g = 0, lu = 0;
@@ -320,10 +331,11 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
           if (j == 0 && lu > 0 && !mbar_wait(&sm.o_empty[t], (lu - 1) & 1, abort, 214)) { ok = false; break; }
           tc_fence_after();
           const uint32_t vb = smem_u32(v_tile(sb, t));
+          const uint32_t p_tmem = p_tmem0 + (gg % NPB) * 32;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, j > 0 || kk > 0);
-          mma_commit(&sm.pv_done[t]);
+          mma_commit(&sm.pv_done[t][gg % NPB]);
           if (j == nkb - 1) mma_commit(&sm.o_full[t]);
           mma_commit(&sm.b_empty[sb]);
         }
@@ -343,44 +355,18 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       coords(u, q0, row0, h);
       float m_use = 0.f;
       for (int j = 0; j < nkb; ++j) {
-        const int gg = g + j, sb = gg % NB;
+        const int gg = g + j;
         if (!mbar_wait(&sm.s_full[t], gg & 1, abort, 206)) { ok = false; break; }
-        if (!mbar_wait(&sm.bias_full[gg & 1], (gg >> 1) & 1, abort, 210)) { ok = false; break; }
         tc_fence_after();
-        // x = S + bias, in two halves of 32 keys (keeps the live registers down)
         uint32_t x[32];
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t sv[16], bb[16];
-          tmem_ld_s_bias_half(lane_addr + Cfg::S_COL + t * 64 + hf * 32, lane_addr + Cfg::BIAS_COL + (gg & 1) * 32 + hf * 16,
-                              sv, bb);
-#pragma unroll
-          for (int c = 0; c < 16; ++c) x[hf * 16 + c] = hadd2_u(sv[c], bb[c]);
-        }
-        // S and the bias stage consumed: QK^T of the next block and the next bias copy may proceed
+        tmem_ld64_pack16(lane_addr + Cfg::S_COL + t * 64, x);
+        // S consumed: the S MMAs of the next block may proceed
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.s_free[t]);
-          mbar_arrive(&sm.bias_empty[gg & 1]);
-        }
-        if (has_mask) {
-          // penalty row of this tile's pair row (0 or -inf per key; the same 128 bytes
-          // for every thread: broadcast reads)
-          if (!mbar_wait(&sm.b_full[sb], (gg / NB) & 1, abort, 216)) { ok = false; break; }
-          const uint4* pen = reinterpret_cast<const uint4*>(sm.ring_b[sb] + Cfg::PEN_OFF + t * 128);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 p = pen[c];
-            x[4 * c] = hadd2_u(x[4 * c], p.x);
-            x[4 * c + 1] = hadd2_u(x[4 * c + 1], p.y);
-            x[4 * c + 2] = hadd2_u(x[4 * c + 2], p.z);
-            x[4 * c + 3] = hadd2_u(x[4 * c + 3], p.w);
-          }
-        }
+        if (lane == 0) mbar_arrive(&sm.s_free[t]);
         const int nvalid = a.Nk - j * BK;
         if (nvalid < BK) {
-          // keys past Nk (zero-filled K and bias) are out of range: -inf
+          // keys past Nk (zero-filled K, bias and penalty) are out of range: -inf
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const uint32_t keep = (2 * c < nvalid ? 0x0000FFFFu : 0u) | (2 * c + 1 < nvalid ? 0xFFFF0000u : 0u);
@@ -395,16 +381,15 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
 #pragma unroll
           for (int c = 0; c < w; ++c) mt[c] = hmax2_u(mt[c], mt[c + w]);
         const float mx = fmaxf(f16lo(mt[0]), f16hi(mt[0]));
-        // P(j) overwrites P(j-1), and an O rescale needs O stable: both need PV(j-1) done.
-        // The softmax of block j-1 already waited for PV(j-2), so pv_done is at most one
-        // phase behind and the parity wait is exact.
+        // P(gg) reuses the buffer of PV(gg - NPB) and an O rescale needs O stable (PV(gg - 1)
+        // done). The previous unit's PVs are all done (its epilogue waited for o_full).
         bool waited = false;
         if (j == 0) {
           m_use = mx;
         } else {
           const bool need = mx > m_use + 8.0f;
           if (__any_sync(0xffffffffu, need)) {
-            if (!mbar_wait(&sm.pv_done[t], (gg - 1) & 1, abort, 208)) { ok = false; break; }
+            if (!mbar_wait(&sm.pv_done[t][(gg - 1) % NPB], ((gg - 1) / NPB) & 1, abort, 208)) { ok = false; break; }
             waited = true;
             tc_fence_after();
             // m_use = -inf (every key so far masked): O holds only zero-weighted terms
@@ -426,19 +411,17 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
         const float m_sub = m_use == -INFINITY ? 0.0f : m_use;
         const __half2 mh2 = __float2half2_rn(m_sub);
         const uint32_t mh = *reinterpret_cast<const uint32_t*>(&mh2);
-        // about 1/3 of the pairs take the polynomial 2^x on the FMA pipe, the rest the MUFU:
-        // the XU pipe (2 issues per f16 pair) and the FMA pipe then finish together.
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const uint32_t d = hsub2_u(x[c], mh);
           pk[c] = TOPS_POLY_PICK(c) ? ex2_poly_f16x2(d) : ex2_f16x2(d);
         }
-        if (j > 0 && !waited) {
-          if (!mbar_wait(&sm.pv_done[t], (gg - 1) & 1, abort, 209)) { ok = false; break; }
+        if (j >= NPB && !waited) {
+          if (!mbar_wait(&sm.pv_done[t][gg % NPB], ((gg - NPB) / NPB) & 1, abort, 209)) { ok = false; break; }
           tc_fence_after();
         }
-        tmem_st32(lane_addr + Cfg::P_COL + t * 32, pk);
+        tmem_st32(lane_addr + Cfg::P_COL + (t * NPB + gg % NPB) * 32, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();

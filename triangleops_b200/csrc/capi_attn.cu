@@ -145,6 +145,9 @@ int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void
 
 // TR rows share one bias tile (TR > 1 only pays off when many rows share the bias).
 // pen: the [R][Nkp] f16 key-penalty rows (0 / -inf), or NULL when no key is masked.
+#ifndef TOPS_ATTN_TR
+#define TOPS_ATTN_TR 3
+#endif
 template <int TR>
 int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
              const void* pen, const void* bias, void* out, cudaStream_t st, int q_head_rows = 0) {
@@ -257,7 +260,7 @@ extern "C" int tops_triangle_attn_attend(int dtype, int64_t R, int64_t N, int64_
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   if (pen_ws != nullptr && !aligned16(pen_ws)) return TOPS_ERR_ALIGN;
   const int n = static_cast<int>(N);
-  return run_attn<3>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
+  return run_attn<TOPS_ATTN_TR>(dtype, static_cast<int>(D), static_cast<int>(R), static_cast<int>(H), n, n, (n + 7) & ~7,
                         q_ws, k_ws, vt_ws, pen_ws, bias_ws, o_out, static_cast<cudaStream_t>(stream));
 }
 
@@ -297,3 +300,4 @@ extern "C" int tops_fused_gate_residual(int dtype, int64_t T_, int64_t C, const 
   return run_gate(dtype, T_, C, o, gin, wg, wo, bg, bo, out, static_cast<cudaStream_t>(stream), residual,
                   static_cast<int>(trans_n));
 }
+

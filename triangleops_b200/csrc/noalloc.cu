@@ -20,7 +20,10 @@
 //     streams) race on the array and corrupt each other's results.
 //   * The first call on a device looks up the array's device address with that
 //     device current (cudaGetSymbolAddress). Make that first call before any CUDA
-//     stream capture.
+//     stream capture. The address is cached per device for the life of the process:
+//     after cudaDeviceReset (or anything else that destroys and recreates the
+//     device's primary context) the cached address is stale, so do not call this
+//     entry point again in such a process.
 #include <cuda_runtime.h>
 #include <mutex>
 #include "sm100.cuh"

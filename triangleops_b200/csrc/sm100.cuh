@@ -74,6 +74,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+#ifndef TOPS_WAIT_SUSPEND_NS
+#define TOPS_WAIT_SUSPEND_NS 0
+#endif
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or the hint elapses, without taking issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(TOPS_WAIT_SUSPEND_NS)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait. `abort` is a CTA-shared flag: once any waiter in the CTA has
 // timed out, every later wait returns false immediately so the CTA drains fast.
 #ifndef TOPS_WAIT_BACKOFF_NS
@@ -85,10 +102,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   unsigned long long t0 = globaltimer();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (TOPS_WAIT_SUSPEND_NS > 0) {
+      if (mbar_try_wait_suspend(bar, parity)) return true;
+    } else if (mbar_try_wait(bar, parity)) {
+      return true;
+    }
     // past a few polls, back off: a warp that spins on a barrier takes issue slots from
     // the warps on its scheduler that do the work
-    if (kWaitBackoffNs > 0 && spins > 4) __nanosleep(kWaitBackoffNs);
+    if (TOPS_WAIT_SUSPEND_NS == 0 && kWaitBackoffNs > 0 && spins > 4) __nanosleep(kWaitBackoffNs);
     if ((++spins & 255u) == 0) {
       if (abort != nullptr && *abort) return false;
       if (globaltimer() - t0 > kWaitTimeoutNs) {
