@@ -38,6 +38,9 @@ sys.path.insert(0, ROOT)
 
 N_DEF, H, D, C = 2048, 4, 32, 128
 REF_H100_MS = 84.35  # reference README.md:60 (triangle_attention N=2048, H100 PCIe)
+# DRAM bytes (read + write) of one attn_kernel launch at N=2048: an ncu capture at N=1024
+# (1.0770 GB, one pass) scaled by rows x keys (x4); the traffic equals the algorithmic bytes
+ATTN_DRAM_BYTES_N2048 = 4.3078e9
 
 
 def _peaks():
@@ -122,7 +125,7 @@ class Clocks:
 def cpu_oracle_ms(inp, N, threads):
     """fp32 torch oracle on the host: two bounded samples (4 and 20 pair rows, each
     including the full-N LN + bias that every row shares), extrapolated linearly to
-    all N rows. Returns (ms_per_call, sample description)."""
+    all N rows. Returns (ms_per_call, sample description, the 20 oracle output rows)."""
     from oracle import oracle
 
     torch.set_num_threads(threads)
@@ -130,10 +133,12 @@ def cpu_oracle_ms(inp, N, threads):
     args = (cpu["X"], cpu["W_ln"], cpu["B_ln"], cpu["WQ"], cpu["WK"], cpu["WV"], cpu["W_proj_z"], None,
             cpu["W_proj_g"], None, cpu["W_proj_o"], None, H, D)
 
+    out = {}
+
     def run(k):
         t0 = time.perf_counter()
-        oracle.triangle_attention_chunked(*args, scale=1 / math.sqrt(D), mask=cpu["mask"], rows=list(range(k)),
-                                          row_block=k)
+        out[k] = oracle.triangle_attention_chunked(*args, scale=1 / math.sqrt(D), mask=cpu["mask"],
+                                                   rows=list(range(k)), row_block=k)
         return time.perf_counter() - t0
 
     ka, kb = 4, 20
@@ -142,29 +147,40 @@ def cpu_oracle_ms(inp, N, threads):
     shared = max(ta - ka * per_row, 0.0)
     ms = (shared + N * per_row) * 1e3
     return ms, (f"oracle.triangle_attention_chunked fp32 on {threads} threads: full-N LN+bias plus {ka} and {kb} "
-                f"of {N} pair rows ({ta:.1f}s, {tb:.1f}s), extrapolated linearly in rows")
+                f"of {N} pair rows ({ta:.1f}s, {tb:.1f}s), extrapolated linearly in rows"), out[kb]
 
 
 def run_reference(args):
+    """The reference arm: the reference algorithm's CPU implementation (the oracle port
+    of references.py:143-277, all host threads) on this workload. One full call over all
+    N pair rows is timed end to end (about half a minute at N=2048) after a bounded
+    warm-up sample; that measured call is the line's value (``steps`` reports the one
+    timed call). The linear extrapolation from 4- and 20-row samples is reported beside it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from oracle import oracle
+
     N = args.n
     threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     inp = make_inputs(N, "cpu")
-    vals = []
-    sample = ""
-    for i in range(args.warmup + args.steps):
-        ms, sample = cpu_oracle_ms(inp, N, threads)
-        if i >= args.warmup:
-            vals.append(ms)
-    v = sorted(vals)[len(vals) // 2]
+    extrap, sample, _ = cpu_oracle_ms(inp, N, threads)  # also the warm-up
+    t0 = time.perf_counter()
+    oracle.triangle_attention_chunked(inp["X"], inp["W_ln"], inp["B_ln"], inp["WQ"], inp["WK"], inp["WV"],
+                                      inp["W_proj_z"], None, inp["W_proj_g"], None, inp["W_proj_o"], None, H, D,
+                                      scale=1 / math.sqrt(D), mask=inp["mask"], row_block=32)
+    v = (time.perf_counter() - t0) * 1e3
+    desc = (f"oracle.triangle_attention_chunked fp32 on {threads} threads, one full call over all {N} pair rows "
+            f"(measured); the 4/20-row extrapolation gives {extrap:.0f} ms")
     line = {"impl": "reference", "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)", "value": v,
-            "unit": "ms", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": v,
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": v / REF_H100_MS, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128, "
-                                                       "mask Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)"},
-            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
+            "unit": "ms", "n_gpus": args.gpus, "steps": 1, "warmup": 1, "steps_requested": args.steps,
+            "ms_per_step": v, "higher_is_better": False, "scaling": "strong", "vs_baseline": v / REF_H100_MS,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128, "
+                                   "mask Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)"},
+            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": "port", "sample": desc,
+                             "extrapolated_ms": extrap, "extrapolation_sample": sample},
             "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -275,23 +291,31 @@ def time_op(fn, iters=10, warmup=3):
     return s.elapsed_time(e) / iters
 
 
-def other_ops(dev):
-    """Config 3 (triangle_mul incoming L=2048) and config 2 (apb M=1024, masked tail)."""
-    import triangleops_b200 as tops
-
-    out = {}
+def config3_inputs(dev, L=2048):
+    """Config 3 generator: triangle_mul incoming, x~N(0,1) (1, L, L, C) bf16, mask =
+    outer(v, v) with v = 1 for the first 1900/2048 of the residues, weights as config 0
+    (LN 1+0.1N / 0.1N, linears N(0, 1/fan_in)), seed 3. Returns (x, mask, weights list
+    in triangle_mul.precompute order)."""
     g = torch.Generator(device=dev).manual_seed(3)
 
     def rn(*s, sd=1.0):
         return (torch.randn(*s, generator=g, device=dev) * sd).to(torch.bfloat16)
 
-    L = 2048
     x = rn(1, L, L, C)
     v = torch.zeros(L, device=dev)
-    v[:1900] = 1
+    v[: L * 1900 // 2048] = 1
     mask = (v[:, None] * v[None, :])[None]
     w = [1 + 0.1 * rn(C), 0.1 * rn(C), rn(2 * C, C, sd=C**-0.5), rn(2 * C, C, sd=C**-0.5), 1 + 0.1 * rn(C),
          0.1 * rn(C), rn(C, C, sd=C**-0.5), rn(C, C, sd=C**-0.5)]
+    return x, mask, w
+
+
+def other_ops(dev):
+    """Config 3 (triangle_mul incoming L=2048) and config 2 (apb M=1024, masked tail)."""
+    import triangleops_b200 as tops
+
+    out = {}
+    x, mask, w = config3_inputs(dev)
     pre = tops.triangle_mul.precompute(*w)
     ms = time_op(lambda: tops.triangle_mul.forward(x, pre, direction="incoming", mask=mask))
     flops = 3.02e12
@@ -325,11 +349,9 @@ def other_ops(dev):
     return out
 
 
-def chain_op(dev, N=2048):
-    """Config 4: tri_mul out -> tri_mul in -> tri_attn start -> tri_attn end (transposed
-    view), x += op(x), ones mask, per-op parameters from seeds 10-13. The fused chain
-    updates x in place (so x drifts over the timed calls; every call does the same work)."""
-    import triangleops_b200 as tops
+def chain_inputs(dev, N=2048):
+    """Config 4 generator: per-op parameters from seeds 10-13 (tri_mul out, tri_mul in,
+    tri_attn start, tri_attn end) and x~N(0,1) (N, N, C) bf16 from seed 4."""
 
     def params(seed, kind):
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -342,9 +364,20 @@ def chain_op(dev, N=2048):
                     WV=rn(C, C, sd=C**-0.5), W_proj_z=rn(C, H, sd=C**-0.5), B_proj_z=None,
                     W_proj_g=rn(C, C, sd=C**-0.5), W_proj_o=rn(C, C, sd=C**-0.5), H=H, D=D)
 
-    pre = tops.pairformer.precompute(params(10, "tm"), params(11, "tm"), params(12, "ta"), params(13, "ta"))
+    ps = (params(10, "tm"), params(11, "tm"), params(12, "ta"), params(13, "ta"))
     g = torch.Generator(device=dev).manual_seed(4)
     x = (torch.randn(N, N, C, generator=g, device=dev)).to(torch.bfloat16)
+    return ps, x
+
+
+def chain_op(dev, N=2048):
+    """Config 4: tri_mul out -> tri_mul in -> tri_attn start -> tri_attn end (transposed
+    view), x += op(x), ones mask, per-op parameters from seeds 10-13. The fused chain
+    updates x in place (so x drifts over the timed calls; every call does the same work)."""
+    import triangleops_b200 as tops
+
+    params, x = chain_inputs(dev, N)
+    pre = tops.pairformer.precompute(*params)
     mask = torch.ones(N, N, dtype=torch.bool, device=dev)
     ms = time_op(lambda: tops.pairformer.pair_update(x, pre, mask=mask), iters=5, warmup=3)
     ms_unfused = time_op(lambda: tops.pairformer.pair_update_unfused(x, pre, mask=mask), iters=3, warmup=2)
@@ -432,21 +465,13 @@ def main():
     mask = inp["mask"][r0:r1].contiguous()
     scale = 1 / math.sqrt(D)
     stream = torch.cuda.current_stream()
-    ev_a0, ev_a1 = [], []
+    kw = dict(scale=scale, W_proj_g=inp["W_proj_g"], W_proj_o=inp["W_proj_o"])
 
-    def step(record=False):
-        ws = K.project_rows(X, pre["W_qkvz"], pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=N, mask_rows=mask,
-                            scale=scale)
-        bias_full = tdist.all_gather_rows(ws["bias"], 1) if world > 1 else ws["bias"]
-        if record:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        O = K.attend_rows(ws, bias_full, H, D)
-        if record:
-            e1.record(stream)
-            ev_a0.append(e0)
-            ev_a1.append(e1)
-        return K.gate_forward(O, ws["xln"], inp["W_proj_g"], inp["W_proj_o"])
+    def step():
+        # the public API call a user makes (one triangle attention over the pair rows)
+        if world > 1:
+            return tdist.triangle_attention_rows(X, pre, N=N, mask_rows=mask, **kw)
+        return tops.triangle_attn.forward(X, pre, mask=mask, B_proj_g=None, B_proj_o=None, **kw)
 
     def barrier():
         if world > 1:
@@ -456,20 +481,31 @@ def main():
     clocks = Clocks(local)
     clocks.start()  # sampling covers warm-up and the timed steps (the timed region alone can be < 1 s)
     time.sleep(1.0)
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, 3)):
         step()
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        step(record=True)
+        step()
     t1.record(stream)
     barrier()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a0, ev_a1)) / args.steps
 
-    # end to end through the public API from pinned host buffers
+    # the attention kernel alone (plus its dead-row vote), on the stream it is launched on,
+    # over the same rows: the roofline figure
+    ws = K.project_rows(X, pre["W_qkvz"], pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=N, mask_rows=mask,
+                        scale=scale)
+    bias_full = tdist.all_gather_rows(ws["bias"], 1) if world > 1 else ws["bias"]
+    attn_ms = time_op(lambda: K.attend_rows(ws, bias_full, H, D), iters=max(3, min(args.steps, 10)), warmup=3)
+    del ws, bias_full
+
+    # parity of this run's output against the fp32 oracle on sampled rows (rank 0 rows)
+    out_rows = step()[: min(n, 20)].float().cpu() if rank == 0 else None
+
+    # end to end through the public API from pinned host buffers: H2D of x and the mask,
+    # forward, D2H of the output, every call
     X_h = X.cpu().pin_memory()
     m_h = mask.cpu().pin_memory()
     out_h = torch.empty(n, N, C, dtype=torch.bfloat16).pin_memory()
@@ -478,11 +514,9 @@ def main():
         Xd = X_h.to(dev, non_blocking=True)
         md = m_h.to(dev, non_blocking=True)
         if world > 1:
-            o = tdist.triangle_attention_rows(Xd, pre, N=N, mask_rows=md, scale=scale, W_proj_g=inp["W_proj_g"],
-                                              W_proj_o=inp["W_proj_o"])
+            o = tdist.triangle_attention_rows(Xd, pre, N=N, mask_rows=md, **kw)
         else:
-            o = tops.triangle_attn.forward(Xd, pre, mask=md, scale=scale, W_proj_g=inp["W_proj_g"], B_proj_g=None,
-                                           W_proj_o=inp["W_proj_o"], B_proj_o=None)
+            o = tops.triangle_attn.forward(Xd, pre, mask=md, B_proj_g=None, B_proj_o=None, **kw)
         out_h.copy_(o, non_blocking=True)
 
     def timed(fn, iters, finish=None):
@@ -502,8 +536,19 @@ def main():
         return e0.elapsed_time(e1) / iters
 
     e2e_iters = max(3, min(args.steps, 5))
+    # single-call latency: one call at a time, each waited for
+    lat = []
+    for _ in range(e2e_iters + 1):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        e2e_step()
+        e1.record(stream)
+        barrier()
+        lat.append(e0.elapsed_time(e1))
+    e2e_latency_ms = sorted(lat[1:])[len(lat[1:]) // 2]
     e2e_serial_ms = timed(e2e_step, e2e_iters)
-    e2e_ms, e2e_method = e2e_serial_ms, "serial: H2D, forward, D2H per call"
+    e2e_ms, e2e_method = e2e_serial_ms, "serial: H2D, forward, D2H per call, back to back"
     if n % 8 == 0:
         # the host-tensor API: row slabs stream in and out on copy streams, and the copies of
         # consecutive calls overlap (PCIe is full duplex); with P ranks each pipes its own
@@ -511,48 +556,56 @@ def main():
         pipe = tops.triangle_attn.HostPipeline(pre, W_proj_g=inp["W_proj_g"], W_proj_o=inp["W_proj_o"],
                                                scale=scale)
         e2e_ms = timed(lambda: pipe(X_h, m_h, out_h), e2e_iters, finish=pipe.wait)
-        e2e_method = "triangle_attn.HostPipeline: slab-streamed H2D/D2H overlapping compute and consecutive calls"
+        e2e_method = ("triangle_attn.HostPipeline, calls back to back (throughput): slab-streamed H2D/D2H "
+                      "overlapping compute and consecutive calls")
 
     if world > 1:
-        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
+        t = torch.tensor([ms, attn_ms, e2e_ms, e2e_latency_ms, e2e_serial_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, attn_ms, e2e_ms = t.tolist()
-
+        ms, attn_ms, e2e_ms, e2e_latency_ms, e2e_serial_ms = t.tolist()
     bf16_burst, bf16_sus, hbm, src = _peaks()
     attn_flops = 4.0 * n * N * N * H * D  # QK^T + PV for this rank's rows
     achieved = attn_flops / attn_ms / 1e9  # TFLOP/s
-    line = None
     if rank == 0:
         ops = other_ops(dev) if (world == 1 and not args.no_ops) else None
-        cpu = None
+        cpu = parity = None
         if world == 1 and not args.no_cpu:
             threads = os.cpu_count() or 1
-            cms, sample = cpu_oracle_ms(inp, N, threads)
+            cms, sample, ref_rows = cpu_oracle_ms(inp, N, threads)
             cpu = {"value": cms, "unit": "ms", "cores": threads, "kind": "port", "sample": sample}
-        # DRAM bytes per attention launch from ncu at N=1024 (profiles/
-        # attn_kernel_triangle_attention_n1024.md: 822.8 MB read + 254.1 MB written), scaled by
-        # rows x keys (n * N) — the kernel streams Q/K/V once and writes O once.
-        traffic = 1.0769e9 * (n * N) / (1024 * 1024)
+            k = min(len(ref_rows), len(out_rows))
+            d = (out_rows[:k] - ref_rows[:k]).abs()
+            parity = {"rows": k, "vs": "fp32 oracle (oracle.triangle_attention_chunked)",
+                      "max_abs": d.max().item(), "mean_abs": d.mean().item(),
+                      "cos": torch.nn.functional.cosine_similarity(out_rows[:k].flatten().double(),
+                                                                   ref_rows[:k].flatten().double(), dim=0).item()}
         line = {
             "metric": f"triangle_attention ms/call (N={N}, H=4, D=32, C=128)",
-            "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": ms / REF_H100_MS if N == 2048 else None,
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"triangle_attention starting-node N={N} H=4 D=32 C=128 bf16, mask "
                                    "Bernoulli(0.9), seed 1 (BASELINE config 1 at N=2048)",
+                       "timed_call": "triangle_attn.forward (public API; the row-slab wrapper with P ranks)",
                        "parallelism": f"row-slab x{world}, bias all-gather" if world > 1 else "single GPU",
                        "l2": "inputs (1 GiB pair tensor) exceed the 126 MB L2; no flush needed",
                        "vs_baseline_ref": "reference 84.35 ms on H100 PCIe (README.md:60)"},
             "roofline": {"bound": "tensor", "kernel": "attn_kernel (QK^T + PV on tcgen05)",
-                         "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s", "frac": achieved / bf16_sus,
-                         "peak_kind": f"{src} sustained bf16", "frac_of_burst": achieved / bf16_burst,
-                         "kernel_ms": attn_ms, "traffic": traffic},
+                         "achieved": achieved, "peak": bf16_burst, "unit": "TFLOP/s", "frac": achieved / bf16_burst,
+                         "peak_kind": f"{src} burst bf16 (the kernel is timed alone, seconds at most)",
+                         "frac_of_sustained": achieved / bf16_sus, "kernel_ms": attn_ms,
+                         "flops_per_launch": attn_flops,
+                         "traffic": ATTN_DRAM_BYTES_N2048 * (n * N) / (2048 * 2048),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one attn_kernel "
+                                           "launch at N=1024 scaled by N^2 (profiles/attn_kernel_dram_n1024.txt)"},
             "e2e": {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": X_h.numel() * 2 + m_h.numel(),
                     "d2h_bytes_per_step": out_h.numel() * 2, "method": e2e_method,
-                    "serial_value": e2e_serial_ms},
-            "gpu_launches": 3 * args.steps,
+                    "latency_ms": e2e_latency_ms, "serial_ms": e2e_serial_ms,
+                    "h2d_d2h_gbs_at_throughput": (X_h.numel() * 2 + m_h.numel() + out_h.numel() * 2) / e2e_ms / 1e6},
+            "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clk,
             "op_tflops": 5.09e12 * (N / 2048) ** 3 / ms / 1e9,
         }

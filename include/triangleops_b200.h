@@ -47,6 +47,10 @@ int tops_device_error(void* stream, int* site);
 /* Single-tile check of one tcgen05 operand mode (0..3) against the host:
  * d (fp32) = A B^T in the layout of that mode. Library self-test. */
 int tops_selftest_umma(int mode, const void* a, const void* b, float* d, void* stream);
+/* 2^x of n f16 values (x_f16) by the two paths of the attention softmax: the FMA-pipe
+ * polynomial (poly_f16) and the MUFU ex2.approx.f16x2 (mufu_f16). Library self-test;
+ * no counterpart in the reference (whose Triton kernels use exp2 in fp32). */
+int tops_selftest_ex2(const void* x_f16, void* poly_f16, void* mufu_f16, int64_t n, void* stream);
 
 /* ---------------------------------------------------------------------------
  * triangle attention (starting node)

@@ -148,7 +148,15 @@ def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, io_roun
     w = {k: _f32(v)[0] for k, v in w.items()}
     C = x.shape[-1]
     xln = F.layer_norm(x, (C,), w["norm_in_weight"], w["norm_in_bias"], eps=eps)
-    g = F.linear(xln, w["p_in_weight"]) * F.linear(xln, w["g_in_weight"]).sigmoid()
+    if io_round is None:
+        lin_in = lambda name: F.linear(xln, w[name])  # noqa: E731
+    else:
+        # the reference folds the LayerNorm affine into each projection and stores the
+        # folded weight in the IO dtype (triangle_mul/module.py:34-38,
+        # _common/ln_absorption.py:28-63): LN(x) W^T = xhat (W*gamma)^T + W beta
+        xhat = F.layer_norm(x, (C,), None, None, eps=eps)
+        lin_in = lambda name: _folded_linear(xhat, w[name], w["norm_in_weight"], w["norm_in_bias"], io_round)  # noqa
+    g = lin_in("p_in_weight") * lin_in("g_in_weight").sigmoid()
     if mask is not None:
         g = g * mask.detach().to("cpu", torch.float32).unsqueeze(-1)
     g = _rt(g, io_round)
@@ -158,8 +166,19 @@ def triangle_multiplicative_update(x, *, direction, mask=None, eps=1e-5, io_roun
     else:
         y = torch.einsum("bkid,bkjd->bijd", a, b)
     y = _rt(y, io_round)
-    yln = F.layer_norm(y, y.shape[-1:], w["norm_out_weight"], w["norm_out_bias"], eps=eps)
-    return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
+    if io_round is None:
+        yln = F.layer_norm(y, y.shape[-1:], w["norm_out_weight"], w["norm_out_bias"], eps=eps)
+        return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
+    yhat = F.layer_norm(y, y.shape[-1:], None, None, eps=eps)
+    p = _folded_linear(yhat, w["p_out_weight"], w["norm_out_weight"], w["norm_out_bias"], io_round)
+    return p * lin_in("g_out_weight").sigmoid()
+
+
+def _folded_linear(xhat, W, gamma, beta, io):
+    """xhat (W*gamma)^T + W beta with the folded weight rounded to ``io`` (the
+    reference's absorb_ln with weight_dtype = the IO dtype)."""
+    Wc = (W * gamma[None, :]).to(io).float()
+    return F.linear(xhat, Wc) + torch.mv(W, beta)
 
 
 def triangle_multiplicative_update_rows(x, *, direction, rows, mask=None, eps=1e-5, **w):

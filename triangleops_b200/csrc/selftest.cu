@@ -180,3 +180,32 @@ extern "C" int tops_selftest_umma(int mode, const void* a, const void* b, float*
   }
   return cudaGetLastError() == cudaSuccess ? TOPS_OK : TOPS_ERR_CUDA;
 }
+
+namespace tops {
+// 2^x of n f16 values by the two paths the attention softmax uses: the polynomial on
+// the FMA pipe (ex2_poly_f16x2) and the MUFU (ex2.approx.f16x2).
+__global__ void selftest_ex2_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ poly,
+                                    uint16_t* __restrict__ mufu, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (2 * i >= n) return;
+  const uint32_t lo = x[2 * i], hi = 2 * i + 1 < n ? x[2 * i + 1] : 0u;
+  const uint32_t v = lo | (hi << 16);
+  const uint32_t p = ex2_poly_f16x2(v), m = ex2_f16x2(v);
+  poly[2 * i] = static_cast<uint16_t>(p & 0xFFFFu);
+  mufu[2 * i] = static_cast<uint16_t>(m & 0xFFFFu);
+  if (2 * i + 1 < n) {
+    poly[2 * i + 1] = static_cast<uint16_t>(p >> 16);
+    mufu[2 * i + 1] = static_cast<uint16_t>(m >> 16);
+  }
+}
+}  // namespace tops
+
+extern "C" int tops_selftest_ex2(const void* x_f16, void* poly_f16, void* mufu_f16, int64_t n, void* stream) {
+  if (n <= 0 || n >= (int64_t(1) << 30)) return TOPS_ERR_SHAPE;
+  if (x_f16 == nullptr || poly_f16 == nullptr || mufu_f16 == nullptr) return TOPS_ERR_ARG;
+  const int pairs = static_cast<int>((n + 1) / 2);
+  tops::selftest_ex2_kernel<<<(pairs + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x_f16), static_cast<uint16_t*>(poly_f16), static_cast<uint16_t*>(mufu_f16),
+      static_cast<int>(n));
+  return cudaGetLastError() == cudaSuccess ? TOPS_OK : TOPS_ERR_CUDA;
+}
