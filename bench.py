@@ -389,8 +389,9 @@ def chain_op(dev, N=2048):
 
 
 def profile_op(args):
-    """Run one of the other ops alone (for ncu captures): triangle_mul incoming at L = --n
-    (config 3 generator) or attn_pair_bias at M = --n (config 2 generator)."""
+    """Run one op alone (for ncu captures): the attention kernel over projected
+    workspaces at N = --n (config 1 generator), triangle_mul incoming at L = --n (config 3
+    generator) or attn_pair_bias at M = --n (config 2 generator)."""
     import triangleops_b200 as tops
 
     dev = torch.device("cuda", 0)
@@ -400,7 +401,17 @@ def profile_op(args):
         return (torch.randn(*s, generator=g, device=dev) * sd).to(torch.bfloat16)
 
     n = args.n
-    if args.profile_op == "triangle_mul":
+    if args.profile_op == "attn_kernel":
+        # the attention kernel alone over projected workspaces (config 1 generator at N = --n)
+        from triangleops_b200.triangle_attn import kernel as K
+
+        inp = make_inputs(n, dev)
+        pre = tops.triangle_attn.precompute(inp["W_ln"], inp["B_ln"], inp["WQ"], inp["WK"], inp["WV"],
+                                            inp["W_proj_z"], None, H, D)
+        ws = K.project_rows(inp["X"], pre["W_qkvz"], pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=n,
+                            mask_rows=inp["mask"], scale=1 / math.sqrt(D))
+        fn = lambda: K.attend_rows(ws, ws["bias"], H, D)  # noqa: E731
+    elif args.profile_op == "triangle_mul":
         x = rn(1, n, n, C)
         v = torch.zeros(n, device=dev)
         v[: n * 1900 // 2048] = 1
@@ -430,8 +441,9 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEF)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ops", action="store_true", help="skip the other two ops")
-    ap.add_argument("--profile-op", choices=["triangle_mul", "attn_pair_bias"], default=None,
-                    help="run only this op (config 3 / config 2 shapes at --n) for profiling, print its time")
+    ap.add_argument("--profile-op", choices=["attn_kernel", "triangle_mul", "attn_pair_bias"], default=None,
+                    help="run only this op (the attention kernel at config 1, triangle_mul at config 3, "
+                         "attn_pair_bias at config 2; size --n) for profiling, print its time")
     args = ap.parse_args()
     if args.impl == "reference-gpu":
         run_reference_gpu(args)
