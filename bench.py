@@ -24,6 +24,7 @@ oracle port, all host threads) on the same workload and prints its line.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -319,9 +320,10 @@ def other_ops(dev):
     pre = tops.triangle_mul.precompute(*w)
     ms = time_op(lambda: tops.triangle_mul.forward(x, pre, direction="incoming", mask=mask))
     flops = 3.02e12
-    _, sus, _, _ = _peaks()
+    burst, sus, _, _ = _peaks()
     out["triangle_multiplicative_update"] = {"config": "incoming L=2048 C=128 bf16, mask tail 1900", "ms": ms,
-                                             "tflops": flops / ms / 1e9, "frac_of_sustained_bf16": flops / ms / 1e9 / sus}
+                                             "tflops": flops / ms / 1e9, "frac_of_burst_bf16": flops / ms / 1e9 / burst,
+                                             "frac_of_sustained_bf16": flops / ms / 1e9 / sus}
     del x, mask
     g2 = torch.Generator(device=dev).manual_seed(2)
 
@@ -382,10 +384,58 @@ def chain_op(dev, N=2048):
     ms = time_op(lambda: tops.pairformer.pair_update(x, pre, mask=mask), iters=5, warmup=3)
     ms_unfused = time_op(lambda: tops.pairformer.pair_update_unfused(x, pre, mask=mask), iters=3, warmup=2)
     flops = 16.2e12
-    _, sus, _, _ = _peaks()
+    burst, sus, _, _ = _peaks()
     return {"config": "Pairformer pair-update chain N=2048 C=128 bf16 (config 4), ones mask", "ms": ms,
-            "tflops": flops / ms / 1e9, "frac_of_sustained_bf16": flops / ms / 1e9 / sus,
+            "tflops": flops / ms / 1e9, "frac_of_burst_bf16": flops / ms / 1e9 / burst,
+            "frac_of_sustained_bf16": flops / ms / 1e9 / sus,
             "ms_per_op_api_composition": ms_unfused}
+
+
+def sharded_ops(dev, world, rank):
+    """Configs 3 and 4 with P ranks (every rank runs this; times are max over ranks):
+    triangle_mul incoming at L=2048 on the replicated pair tensor (row slabs, b exchanged
+    chunk by chunk under the contraction) and the Pairformer chain on row-sharded x. Plus
+    each collective alone at its per-rank size, so the line names what bounds the curve."""
+    import torch.distributed as dist
+
+    import triangleops_b200 as tops
+    from triangleops_b200 import dist as tdist
+
+    def tmax(v):
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    out = {}
+    x, mask, w = config3_inputs(dev)
+    pre = tops.triangle_mul.precompute(*w)
+    L = x.shape[1]
+    ms = time_op(lambda: tdist.triangle_multiplicative_update_rows(x, pre, direction="incoming", mask=mask), iters=10)
+    out["triangle_multiplicative_update"] = {"config": f"incoming L={L} C=128 bf16, mask tail 1900, row slabs x{world}",
+                                             "ms": tmax(ms), "tflops": 3.02e12 / tmax(ms) / 1e9}
+    del x, mask
+    params, xc = chain_inputs(dev)
+    N = xc.shape[0]
+    r0, r1 = tdist.slab(N, rank, world)
+    x_rows = xc[r0:r1].contiguous()
+    del xc
+    cpre = tops.pairformer.precompute(*params)
+    ones = torch.ones(N, N, dtype=torch.bool, device=dev)
+    ms = time_op(lambda: tdist.pair_update_rows(x_rows, cpre, mask=ones), iters=5, warmup=3)
+    out["pairformer_pair_update"] = {"config": f"chain N={N} C=128 bf16, ones mask, row slabs x{world}",
+                                     "ms": tmax(ms), "tflops": 16.2e12 / tmax(ms) / 1e9}
+    # the collectives alone, at this run's per-rank sizes
+    n = N // world
+    b = torch.empty(C, L, n, dtype=torch.bfloat16, device=dev)  # one rank's b chunk (incoming)
+    coll = {"trimul_b_exchange_ms": tmax(time_op(lambda: tdist.exchange_chunks(b, rank, world, None,
+                                                                                lambda s, f: None), iters=10)),
+            "attn_bias_allgather_ms": tmax(time_op(lambda: tdist.all_gather_rows(
+                torch.empty(H, n, N, dtype=torch.float16, device=dev), 1), iters=10)),
+            "chain_transpose_ms": tmax(time_op(lambda: tdist.transpose_rows(x_rows), iters=10)),
+            "bytes_per_rank": {"trimul_b": b.numel() * 2 * (world - 1), "attn_bias": H * n * N * 2 * (world - 1),
+                               "transpose": x_rows.numel() * 2 * (world - 1) // world}}
+    out["collectives"] = coll
+    return out
 
 
 def profile_op(args):
@@ -465,7 +515,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        # a short timeout: a collective that cannot complete ends the run in minutes
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     N = args.n
     r0, r1 = tdist.slab(N, rank, world)
     n = r1 - r0
@@ -514,7 +565,9 @@ def main():
     del ws, bias_full
 
     # parity of this run's output against the fp32 oracle on sampled rows (rank 0 rows)
-    out_rows = step()[: min(n, 20)].float().cpu() if rank == 0 else None
+    o = step()  # every rank: the call holds a collective when sharded
+    out_rows = o[: min(n, 20)].float().cpu() if rank == 0 else None
+    del o
 
     # end to end through the public API from pinned host buffers: H2D of x and the mask,
     # forward, D2H of the output, every call
@@ -578,8 +631,12 @@ def main():
     bf16_burst, bf16_sus, hbm, src = _peaks()
     attn_flops = 4.0 * n * N * N * H * D  # QK^T + PV for this rank's rows
     achieved = attn_flops / attn_ms / 1e9  # TFLOP/s
+    ops = None
+    if not args.no_ops and world > 1:
+        ops = sharded_ops(dev, world, rank)
     if rank == 0:
-        ops = other_ops(dev) if (world == 1 and not args.no_ops) else None
+        if not args.no_ops and world == 1:
+            ops = other_ops(dev)
         cpu = parity = None
         if world == 1 and not args.no_cpu:
             threads = os.cpu_count() or 1

@@ -135,6 +135,13 @@ int tops_trimul_contract(int dtype, int direction, int64_t nb, int64_t L, const 
  *   y [nb][Mi][L]. L % P == 0 and (L/P) % 128 == 0 when P > 1; Mi % 8 == 0. */
 int tops_trimul_contract_slab(int dtype, int direction, int64_t nb, int64_t Mi, int64_t L, int64_t P, const void* a,
                               const void* b, void* y, void* stream);
+/* The row-slab contraction restricted to output columns [j_begin, j_begin + j_count) (no
+ * counterpart in the reference): a sharded caller contracts each chunk of b as the
+ * collective delivers it. j_begin % 256 == 0; j_count % 256 == 0 unless the range ends
+ * at L. b is the full chunk buffer; only the chunks covering the range are read. */
+int tops_trimul_contract_slab_cols(int dtype, int direction, int64_t nb, int64_t Mi, int64_t L, int64_t P,
+                                   int64_t j_begin, int64_t j_count, const void* a, const void* b, void* y,
+                                   void* stream);
 /* Output phase — replaces triangle_mul/kernel.py:282-326 (output_phase):
  *   out[m][c] = sigmoid(LN_in(x) g_out^T)[m,c] * (LN_out(y) p_out^T)[m,c]
  *   y [C][M] (D-major), x [M][C]; w_out [2C][C] = p_out_c | g_out_c; sum_out, b_out [2C] fp32;

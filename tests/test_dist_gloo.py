@@ -88,6 +88,17 @@ class CpuTrimulOps:
         b = b_chunks.permute(1, 2, 0, 3).reshape(a.shape[0], L, L)  # (C, k, j)
         return torch.einsum("dki,dkj->dij", a, b)
 
+    COL_TILE = 1  # exercise the chunk-by-chunk exchange on CPU
+
+    @staticmethod
+    def contract_cols(a, b_flat, direction, Mi, L, P, j0, jc, y):
+        C, nc = a.shape[0], L // P
+        ch = b_flat[j0 // nc]  # one chunk: (C, nc, L) outgoing / (C, L, nc) incoming
+        if direction == "outgoing":
+            y[:, :, j0:j0 + jc] = torch.einsum("dik,djk->dij", a, ch)
+        else:
+            y[:, :, j0:j0 + jc] = torch.einsum("dki,dkj->dij", a, ch)
+
     @staticmethod
     def output_phase(y, xt, pre, eps):
         w = pre["w"]
@@ -98,9 +109,9 @@ class CpuTrimulOps:
         return F.linear(yln, w["p_out_weight"]) * F.linear(xln, w["g_out_weight"]).sigmoid()
 
 
-def _trimul_inputs():
+def _trimul_inputs(L=12):
     g = torch.Generator().manual_seed(11)
-    L, C = 8, 16
+    C = 16
     r = lambda *s, sd=1.0: torch.randn(*s, generator=g) * sd  # noqa: E731
     w = dict(norm_in_weight=1 + 0.1 * r(C), norm_in_bias=0.1 * r(C), p_in_weight=r(2 * C, C, sd=C**-0.5),
              g_in_weight=r(2 * C, C, sd=C**-0.5), norm_out_weight=1 + 0.1 * r(C), norm_out_bias=0.1 * r(C),
@@ -121,12 +132,15 @@ def _trimul_worker(rank, world, port, q, direction):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("direction", ["outgoing", "incoming"])
-def test_sharded_triangle_mul_gloo(direction):
+def test_sharded_triangle_mul_gloo(direction, world):
+    """Row slabs with b exchanged chunk by chunk (each peer's chunk contracted as it
+    arrives); 3 ranks exercise steps that pair every rank with two different peers."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_trimul_worker, args=(r, 2, port, q, direction)) for r in range(2)]
+    procs = [ctx.Process(target=_trimul_worker, args=(r, world, port, q, direction)) for r in range(world)]
     for p in procs:
         p.start()
     full = q.get(timeout=120)

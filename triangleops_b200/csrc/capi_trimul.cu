@@ -51,7 +51,8 @@ int launch_trimul_out(int dtype, const void* y, const void* x, const void* w, co
 }
 
 template <typename T, bool MN>
-int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, const void* b, void* y, cudaStream_t st) {
+int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, const void* b, void* y, cudaStream_t st,
+                    int j_begin, int j_end) {
   CUtensorMap ma, mb;
   const int nc = L / P;
   const uint64_t e = 2;
@@ -79,11 +80,11 @@ int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, cons
     if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
     if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
-  CtArgs args{L, nb, y, Mi, nc};
+  CtArgs args{L, nb, y, Mi, nc, j_begin, j_end};
   const size_t smem = sizeof(CtSmem) + 1024;
   auto kern = trimul_contract_kernel<T, MN>;
   set_smem(kern, smem);
-  const long long tiles = static_cast<long long>((Mi + kCtBM - 1) / kCtBM) * ((L + kCtBN - 1) / kCtBN) * nb;
+  const long long tiles = static_cast<long long>((Mi + kCtBM - 1) / kCtBM) * ((j_end - j_begin + kCtBN - 1) / kCtBN) * nb;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
   kern<<<grid, 384, smem, st>>>(ma, mb, args);
   return launch_status();
@@ -113,12 +114,13 @@ int run_trimul_out(int dtype, int C, const void* y, const void* x, const void* w
 }
 
 int run_contract(int dtype, int direction, int nb, int Mi, int L, int P, const void* a, const void* b, void* y,
-                 cudaStream_t st) {
+                 cudaStream_t st, int j_begin = 0, int j_end = -1) {
+  if (j_end < 0) j_end = L;
   if (dtype == TOPS_BF16)
-    return direction == 0 ? launch_contract<__nv_bfloat16, false>(dtype, nb, Mi, L, P, a, b, y, st)
-                          : launch_contract<__nv_bfloat16, true>(dtype, nb, Mi, L, P, a, b, y, st);
-  return direction == 0 ? launch_contract<__half, false>(dtype, nb, Mi, L, P, a, b, y, st)
-                        : launch_contract<__half, true>(dtype, nb, Mi, L, P, a, b, y, st);
+    return direction == 0 ? launch_contract<__nv_bfloat16, false>(dtype, nb, Mi, L, P, a, b, y, st, j_begin, j_end)
+                          : launch_contract<__nv_bfloat16, true>(dtype, nb, Mi, L, P, a, b, y, st, j_begin, j_end);
+  return direction == 0 ? launch_contract<__half, false>(dtype, nb, Mi, L, P, a, b, y, st, j_begin, j_end)
+                        : launch_contract<__half, true>(dtype, nb, Mi, L, P, a, b, y, st, j_begin, j_end);
 }
 
 }  // namespace tops
@@ -167,6 +169,30 @@ extern "C" int tops_trimul_contract_slab(int dtype, int direction, int64_t nb, i
     if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
   return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(Mi), static_cast<int>(L),
                       static_cast<int>(P), a, b, y, static_cast<cudaStream_t>(stream));
+}
+
+// The same contraction restricted to output columns [j_begin, j_begin + j_count): lets a
+// sharded caller contract each chunk of B as soon as the collective has delivered it.
+// j_begin must be a multiple of 256 (the tile width), and so must j_count unless the
+// range ends at L; B is still the full rank-major chunk buffer (only the chunks holding
+// the range are read).
+extern "C" int tops_trimul_contract_slab_cols(int dtype, int direction, int64_t nb, int64_t Mi, int64_t L, int64_t P,
+                                              int64_t j_begin, int64_t j_count, const void* a, const void* b, void* y,
+                                              void* stream) {
+  if (dtype != TOPS_BF16 && dtype != TOPS_F16) return TOPS_ERR_DTYPE;
+  if (direction != 0 && direction != 1) return TOPS_ERR_ARG;
+  if (nb <= 0 || L <= 0 || Mi <= 0 || P <= 0 || Mi > L || nb >= (1 << 30) || L >= (1 << 20)) return TOPS_ERR_SHAPE;
+  if (L % P != 0) return TOPS_ERR_SHAPE;
+  if (L % 8 != 0 || Mi % 8 != 0) return TOPS_ERR_ALIGN;
+  if (P > 1 && (L / P) % 128 != 0) return TOPS_ERR_SHAPE;
+  if (j_begin < 0 || j_count <= 0 || j_begin + j_count > L || j_begin % 256 != 0) return TOPS_ERR_SHAPE;
+  if (j_count % 256 != 0 && j_begin + j_count != L) return TOPS_ERR_SHAPE;
+  const void* ptrs[] = {a, b, y};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return TOPS_ERR_ALIGN;
+  return run_contract(dtype, direction, static_cast<int>(nb), static_cast<int>(Mi), static_cast<int>(L),
+                      static_cast<int>(P), a, b, y, static_cast<cudaStream_t>(stream), static_cast<int>(j_begin),
+                      static_cast<int>(j_begin + j_count));
 }
 
 extern "C" int tops_trimul_output_phase(int dtype, int64_t M, int64_t C, const void* y, const void* x,

@@ -444,6 +444,7 @@ struct CtArgs {
   void* y;  // [nb][Mi][L]
   int Mi;   // rows of A / y (L unsharded; a row slab of size L/P when sharded)
   int nc;   // extent of one B chunk along j (B is P rank-major chunks of nc columns; nc = L unsharded)
+  int j_base, j_end;  // the launch computes output columns [j_base, j_end) only (j_base % kCtBN == 0)
 };
 
 template <typename T, bool MN>
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(384, 1)
   extern __shared__ uint8_t smem_raw[];
   CtSmem& sm = *reinterpret_cast<CtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nI = (a.Mi + kCtBM - 1) / kCtBM, nJ = (a.L + kCtBN - 1) / kCtBN;
+  const int nI = (a.Mi + kCtBM - 1) / kCtBM, nJ = (a.j_end - a.j_base + kCtBN - 1) / kCtBN;
   const long long n_tiles = static_cast<long long>(nI) * nJ * a.nb;
   const int nk = (a.L + kCtBK - 1) / kCtBK;
   if (threadIdx.x == 0) {
@@ -478,7 +479,7 @@ __global__ void __launch_bounds__(384, 1)
     bb = static_cast<int>(tile / per_b);
     const int r = static_cast<int>(tile - static_cast<long long>(bb) * per_b);
     i0 = (r / nJ) * kCtBM;
-    j0 = (r % nJ) * kCtBN;
+    j0 = a.j_base + (r % nJ) * kCtBN;
   };
 
   if (warp == 0) {
@@ -564,13 +565,13 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t p[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) p[e] = E::pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-          if (j0 + c0 + 32 <= a.L) {
+          if (j0 + c0 + 32 <= a.j_end) {
             uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
 #pragma unroll
             for (int q = 0; q < 4; ++q) d4[q] = make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
           } else {
             for (int e = 0; e < 32; ++e)
-              if (j0 + c0 + e < a.L) dst[c0 + e] = E::from_f(__uint_as_float(r[e]));
+              if (j0 + c0 + e < a.j_end) dst[c0 + e] = E::from_f(__uint_as_float(r[e]));
           }
         }
       }

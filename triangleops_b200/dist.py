@@ -92,6 +92,14 @@ def triangle_attention_rows(X_rows, pre, *, N, mask_rows=None, scale=1.0, eps=1e
 class TrimulKernelOps:
     """The sm_100a kernels for one rank's triangle-mul slab."""
 
+    COL_TILE = 256  # contract_cols ranges start on (and span) multiples of this
+
+    @staticmethod
+    def contract_cols(a, b_flat, direction, Mi, L, P, j0, jc, y):
+        from .triangle_mul.kernel import contract_slab_cols
+
+        contract_slab_cols(a, b_flat, direction, Mi, L, P, j0, jc, y)
+
     @staticmethod
     def input_phase(x_tokens, mask_tokens, pre, eps):
         from .triangle_mul.kernel import input_phase_tokens
@@ -111,6 +119,53 @@ class TrimulKernelOps:
         return output_phase_tokens(y, x_tokens, pre, eps)
 
 
+def exchange_chunks(chunk, rank, world, group, on_chunk):
+    """All-gather of equal chunks (rank-major, as all_gather_into_tensor lays them out)
+    that hands each chunk to ``on_chunk(src, flat)`` as soon as it has arrived, the
+    caller's own chunk first. Step s of world-1 pairs every rank r with r+s (send) and
+    r-s (receive); on CUDA the transfers run on a side stream and each on_chunk call is
+    enqueued on the caller's stream behind an event of its transfer, so the work on a
+    chunk overlaps the transfers of the later ones. Returns the filled (world, ...) buffer."""
+    flat = torch.empty((world,) + tuple(chunk.shape), dtype=chunk.dtype, device=chunk.device)
+    flat[rank].copy_(chunk)
+    on_chunk(rank, flat)
+    cuda = chunk.is_cuda
+    if cuda:
+        main = torch.cuda.current_stream(chunk.device)
+        side = _comm_stream(chunk.device)
+        side.wait_stream(main)  # the chunk (and flat) are ready on the caller's stream
+        chunk.record_stream(side)
+        flat.record_stream(side)
+    for step in range(1, world):
+        dst, src = (rank + step) % world, (rank - step) % world
+        if cuda:
+            with torch.cuda.stream(side):
+                reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, chunk, dst, group),
+                                               dist.P2POp(dist.irecv, flat[src], src, group)])
+                for r in reqs:
+                    r.wait()
+                ev = torch.cuda.Event()
+                ev.record(side)
+            main.wait_event(ev)
+        else:
+            for r in dist.batch_isend_irecv([dist.P2POp(dist.isend, chunk, dst, group),
+                                             dist.P2POp(dist.irecv, flat[src], src, group)]):
+                r.wait()
+        on_chunk(src, flat)
+    return flat
+
+
+_COMM = {}
+
+
+def _comm_stream(device):
+    """One side stream per device for the chunked collectives."""
+    key = torch.device(device).index
+    if key not in _COMM:
+        _COMM[key] = torch.cuda.Stream(device=device)
+    return _COMM[key]
+
+
 def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
     """The triangle multiplicative update of this rank's pair rows from its row slab
     x_rows (n, L, C) = x[r0:r1] and, for the incoming direction, its column slab given
@@ -128,13 +183,26 @@ def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
     ab = ops.input_phase(xs.contiguous(), ms, pre, eps)  # (2C, n*L) as [d][i][k] or [d][k][i]
     a = ab[:C].reshape(C, n, L) if direction == "outgoing" else ab[:C].reshape(C, L, n)
     b = ab[C:].reshape(C, n, L) if direction == "outgoing" else ab[C:].reshape(C, L, n)
-    if world > 1:
-        flat = torch.empty((world * b.shape[0],) + tuple(b.shape[1:]), dtype=b.dtype, device=b.device)
-        dist.all_gather_into_tensor(flat, b.contiguous(), group=group)  # rank-major concatenation
-        b_chunks = flat.view((world,) + tuple(b.shape))
+    nc = L // world
+    tile = getattr(ops, "COL_TILE", None)
+    if world > 1 and tile is not None and nc % tile == 0:
+        # b's chunks arrive one peer at a time on a side stream; each chunk's output
+        # columns are contracted as soon as it lands, the rank's own chunk first
+        y = torch.empty(C, n, L, dtype=a.dtype, device=a.device)
+        a = a.contiguous()
+
+        def on_chunk(src, flat):
+            ops.contract_cols(a, flat, direction, n, L, world, src * nc, nc, y)
+
+        exchange_chunks(b.contiguous(), rank, world, group, on_chunk)
     else:
-        b_chunks = b.unsqueeze(0)
-    y = ops.contract_slab(a, b_chunks, direction, n, L, world)  # (C, n, L)
+        if world > 1:
+            flat = torch.empty((world * b.shape[0],) + tuple(b.shape[1:]), dtype=b.dtype, device=b.device)
+            dist.all_gather_into_tensor(flat, b.contiguous(), group=group)  # rank-major concatenation
+            b_chunks = flat.view((world,) + tuple(b.shape))
+        else:
+            b_chunks = b.unsqueeze(0)
+        y = ops.contract_slab(a, b_chunks, direction, n, L, world)  # (C, n, L)
     out = ops.output_phase(y.reshape(C, n * L), x_rows.reshape(n * L, C).contiguous(), pre, eps)
     return out.reshape(n, L, C)
 

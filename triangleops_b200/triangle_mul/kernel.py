@@ -18,6 +18,7 @@ _P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _lib.register("tops_trimul_input_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P])
 _lib.register("tops_trimul_contract", [_I, _I, _I64, _I64, _P, _P, _P, _P])
 _lib.register("tops_trimul_contract_slab", [_I, _I, _I64, _I64, _I64, _I64, _P, _P, _P, _P])
+_lib.register("tops_trimul_contract_slab_cols", [_I, _I, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P])
 _lib.register("tops_trimul_output_phase", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P])
 _lib.register("tops_trimul_output_phase_residual", [_I, _I64, _I64, _P, _P, _P, _P, _P, _F, _P, _P, _P])
 _lib.register("tops_trimul_forward",
@@ -149,6 +150,19 @@ def contract_slab(a, b_chunks, direction, Mi, L, P):
     b_chunks = b_chunks.contiguous()
     _lib.call("tops_trimul_contract_slab", dt, code, C, Mi, L, P, a.data_ptr(), b_chunks.data_ptr(), y.data_ptr(),
               _lib.stream_ptr(a.device))
+    return y
+
+
+def contract_slab_cols(a, b_flat, direction, Mi, L, P, j_begin, j_count, y):
+    """Output columns [j_begin, j_begin + j_count) of :func:`contract_slab` into the
+    caller's y (C, Mi, L); b_flat is the full (P, C, ...) chunk buffer, of which only
+    the chunks covering the range are read."""
+    code = direction_code(direction)
+    C = a.shape[0]
+    dt = _lib.dtype_code(a.dtype)
+    assert y.is_contiguous() and y.shape == (C, Mi, L) and a.is_contiguous() and b_flat.is_contiguous()
+    _lib.call("tops_trimul_contract_slab_cols", dt, code, C, Mi, L, P, j_begin, j_count, a.data_ptr(),
+              b_flat.data_ptr(), y.data_ptr(), _lib.stream_ptr(a.device))
     return y
 
 
