@@ -241,6 +241,16 @@ int tops_f32_attention(int64_t R, int64_t H, int64_t Nq, int64_t Nk, int64_t D, 
 int tops_f32_gated_mul(int64_t rows, int64_t cols, const float* a, int64_t lda, const float* g, int64_t ldg,
                        const float* bg, const uint8_t* mask, float* y, int64_t ldy, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Pairformer pair transition (no counterpart in the reference, which ships only the
+ * triangle ops; the AlphaFold-3 transition layer): over M tokens of C = 128 channels
+ *   out = x + ( silu(LN(x) W1^T) * (LN(x) W2^T) ) W3^T,   hidden width 4C,
+ * with the LN affine folded on the host: w12 [(4C/64) * 128][C] holds, per 64-wide
+ * hidden chunk h, the rows W1[h]*gamma then W2[h]*gamma (IO dtype); b12 [(4C/64)][128]
+ * fp32 the matching W1[h] beta | W2[h] beta; w3 [C][4C] (IO dtype). out may alias x. */
+int tops_transition_forward(int dtype, int64_t M, int64_t C, const void* x, const void* w12, const void* w3,
+                            const float* b12, float eps, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,6 +16,9 @@ implementation of one op (youngchan2/TriangleOps ``benchmarks/references.py``):
 * :func:`pair_update`                     <- the four triangle ops chained with residual adds
   (out, in, starting, ending = transposed view), composed from
   the functions above
+* :func:`transition`                      <- the Pairformer pair transition (no counterpart in
+  the reference, which ships only the triangle ops): the published AlphaFold-3 transition
+  layer, x + W3 (silu(LN(x) W1^T) * (LN(x) W2^T)), hidden width 4C, no biases
 
 plus the LN-affine fold of ``triangle_ops/_common/ln_absorption.py:28-63``
 (:func:`absorb_ln`, :func:`absorb_ln_matmul`).
@@ -252,12 +255,14 @@ def attention_pair_bias_masked(X, WQ, WK, WV, Z, W_ln, B_ln, W_proj_z, B_proj_z,
 # Pairformer pair-update chain (composition of the functions above)
 # --------------------------------------------------------------------------- #
 def pair_update(x, *, tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end, mask=None, scale=None, eps=1e-5,
-                io_round=None, stages=("tri_mul_out", "tri_mul_in", "tri_attn_start", "tri_attn_end")):
+                io_round=None, stages=("tri_mul_out", "tri_mul_in", "tri_attn_start", "tri_attn_end"),
+                transition=None):
     """x (N, N, C) -> x + the four triangle updates in order, fp32 CPU:
     x += trimul_out(x); x += trimul_in(x); x += tri_attn(x); x += tri_attn(x^T)^T with
     mask^T (ending node as the transposed view). ``tri_mul_*``: the eight trimul
     weights; ``tri_attn_*``: W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, W_proj_g,
-    W_proj_o, H, D. ``stages`` selects a sub-sequence. ``io_round`` rounds what a chain in the IO dtype stores: each op's
+    W_proj_o, H, D; ``transition``: the weights of the optional fifth stage
+    "transition" (:func:`transition`). ``stages`` selects a sub-sequence. ``io_round`` rounds what a chain in the IO dtype stores: each op's
     intermediates (the ops' own ``io_round``), each op's output and x after every add."""
     (x,) = _f32(x)
     r = io_round
@@ -279,4 +284,31 @@ def pair_update(x, *, tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end, mas
                                w["W_proj_g"], None, w["W_proj_o"], None, w["H"], w["D"], scale=sc, eps=eps, mask=mm,
                                io_round=r)
         x = _rt(x + _rt(o.transpose(0, 1) if ending else o, r), r)
+    if "transition" in stages:
+        x = _transition_layer(x, eps=eps, io_round=r, **transition)
     return x
+
+
+# --------------------------------------------------------------------------- #
+# Pairformer pair transition (AlphaFold 3 supplementary, Algorithm 11 "Transition")
+# --------------------------------------------------------------------------- #
+def transition(x, *, norm_weight, norm_bias, w1, w2, w3, eps=1e-5, io_round=None):
+    """x (..., C) -> x + transition(x), fp32 CPU: a = LN(x); h = silu(a W1^T) * (a W2^T)
+    with W1, W2 (nC, C); out = x + h W3^T with W3 (C, nC). ``io_round`` rounds what a
+    16-bit kernel stores: the LN-folded weights (W1*gamma, W2*gamma), the hidden h and
+    the output."""
+    (x, norm_weight, norm_bias, w1, w2, w3) = _f32(x, norm_weight, norm_bias, w1, w2, w3)
+    C = x.shape[-1]
+    if io_round is None:
+        a = F.layer_norm(x, (C,), norm_weight, norm_bias, eps=eps)
+        u, v = F.linear(a, w1), F.linear(a, w2)
+    else:
+        xhat = _rt(F.layer_norm(x, (C,), None, None, eps=eps), io_round)
+        u = _folded_linear(xhat, w1, norm_weight, norm_bias, io_round)
+        v = _folded_linear(xhat, w2, norm_weight, norm_bias, io_round)
+        w3 = _rt(w3, io_round)
+    h = _rt(F.silu(u) * v, io_round)
+    return _rt(x + F.linear(h, w3), io_round)
+
+
+_transition_layer = transition  # pair_update's keyword of the same name holds the weights

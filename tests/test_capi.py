@@ -5,6 +5,7 @@ import os
 import re
 
 import pytest
+import torch
 
 from triangleops_b200 import _build, _lib
 
@@ -141,3 +142,21 @@ def test_pairformer_shape_checks_on_host():
         tops.pairformer.pair_update(torch.zeros(10, 10, 128), {}, mask=None)  # N % 8
     with pytest.raises(AssertionError):
         tops.pairformer.pair_update(torch.zeros(8, 8, 128), {}, stages=("tri_mul_sideways",))
+
+
+def test_transition_precompute_on_host():
+    """The transition's host-side weight prep: LN affine folded per hidden chunk."""
+    import triangleops_b200 as tops
+
+    C = 128
+    g = torch.Generator().manual_seed(0)
+    w1, w2 = torch.randn(4 * C, C, generator=g), torch.randn(4 * C, C, generator=g)
+    gamma, beta = torch.randn(C, generator=g), torch.randn(C, generator=g)
+    pre = tops.transition.precompute(gamma, beta, w1, w2, torch.randn(C, 4 * C, generator=g))
+    assert pre["w12"].shape == (8 * C, C) and pre["b12"].shape == (8, 2 * 64)
+    # chunk 3: rows 384..447 of w12 are W1[192:256]*gamma, rows 448..511 W2[192:256]*gamma
+    assert torch.allclose(pre["w12"][384:448], w1[192:256] * gamma)
+    assert torch.allclose(pre["w12"][448:512], w2[192:256] * gamma)
+    assert torch.allclose(pre["b12"][3, :64], w1[192:256] @ beta, atol=1e-4)
+    with pytest.raises(AssertionError):
+        tops.transition.precompute(gamma, beta, w1[:, :64], w2[:, :64], torch.randn(C, 4 * C))

@@ -9,12 +9,13 @@ Drop-in for the ``triangle_ops`` Python API (``triangle_ops/__init__.py:17-31``)
 Each op module exposes ``precompute(...)`` (one-time weight prep -> opaque dict),
 ``forward(x, pre, ...)`` (per call) and the one-shot ``<op_name>(...)``.
 ``pairformer.pair_update`` chains the triangle ops of one Pairformer block
-in place (residual adds fused, ending node without a transpose copy).
+in place (residual adds fused, ending node without a transpose copy);
+``transition`` is the Pairformer pair transition MLP (one fused kernel).
 All compute runs in hand-written sm_100a kernels behind a C-ABI library
 (``libtriangleops_b200.so``); there is no CPU fallback.
 """
 
-from . import attn_pair_bias, pairformer, triangle_attn, triangle_mul
+from . import attn_pair_bias, pairformer, transition, triangle_attn, triangle_mul
 from .attn_pair_bias import attention_pair_bias
 from .triangle_attn import triangle_attention
 from .triangle_mul import triangle_multiplicative_update
@@ -25,6 +26,7 @@ __all__ = [
     "attn_pair_bias",
     "attention_pair_bias",
     "pairformer",
+    "transition",
     "triangle_attn",
     "triangle_mul",
     "triangle_attention",

@@ -5,9 +5,12 @@
     x += triangle_attention(x)                       (starting node)
     x += triangle_attention(x^T)^T                   (ending node)
 
+    x += transition(x)                               (optional stage "transition")
+
 The reference ships the three primitives, not the block; this is the glue a
-Pairformer trunk puts around them (AlphaFold-3-style ordering; the transition MLP
-and the single-representation update are not part of the primitives' path).
+Pairformer trunk puts around them (AlphaFold-3-style ordering). The pair transition
+(:mod:`triangleops_b200.transition`) runs as a fifth stage when its weights are
+given; the single-representation update is not part of the pair path.
 Every residual add is fused into the epilogue of the op's last kernel (the
 triangle-mul output phase, the gate), which writes x in place. The ending node
 reads x column-wise through a 3-D tensor map (no transposed copy) and its gate
@@ -22,13 +25,15 @@ from .triangle_attn import module as _ta
 from .triangle_attn.kernel import attend_rows, gate_forward, project_rows
 from .triangle_mul import module as _tm
 from .triangle_mul.kernel import residual_update
+from . import transition as _tr
 
 
-def precompute(tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end):
+def precompute(tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end, transition=None):
     """Weights of the four ops. ``tri_mul_*``: dicts of the eight
     ``triangle_mul.precompute`` arguments; ``tri_attn_*``: dicts with the
     ``triangle_attn.precompute`` arguments (W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z,
-    H, D) plus W_proj_g and W_proj_o."""
+    H, D) plus W_proj_g and W_proj_o; ``transition`` (optional): a dict of the
+    ``transition.precompute`` arguments (norm_weight, norm_bias, w1, w2, w3)."""
     keys_tm = ("norm_in_weight", "norm_in_bias", "p_in_weight", "g_in_weight", "norm_out_weight", "norm_out_bias",
                "p_out_weight", "g_out_weight")
     keys_ta = ("W_ln", "B_ln", "WQ", "WK", "WV", "W_proj_z", "B_proj_z", "H", "D")
@@ -40,6 +45,8 @@ def precompute(tri_mul_out, tri_mul_in, tri_attn_start, tri_attn_end):
         pre["W_proj_g"] = w["W_proj_g"]
         pre["W_proj_o"] = w["W_proj_o"]
         out[name] = pre
+    if transition is not None:
+        out["transition"] = _tr.precompute(**transition)
     return out
 
 
@@ -56,6 +63,7 @@ def _tri_attn_residual(x, pre, mask, scale, eps, ending):
 
 
 STAGES = ("tri_mul_out", "tri_mul_in", "tri_attn_start", "tri_attn_end")
+ALL_STAGES = STAGES + ("transition",)
 
 
 def pair_update(x, pre, *, mask=None, scale=None, eps=1e-5, stages=STAGES):
@@ -68,13 +76,15 @@ def pair_update(x, pre, *, mask=None, scale=None, eps=1e-5, stages=STAGES):
     assert x4.shape[0] == 1 and x4.is_contiguous(), "one contiguous pair tensor"
     N = x4.shape[1]
     assert N % 8 == 0, "N must be a multiple of 8"
-    assert all(st in STAGES for st in stages), f"stages must be drawn from {STAGES}"
+    assert all(st in ALL_STAGES for st in stages), f"stages must be drawn from {ALL_STAGES}"
     m = None if mask is None else mask.reshape(N, N)
     m3 = None if m is None else m.reshape(1, N, N)
-    for name in STAGES:
+    for name in ALL_STAGES:
         if name not in stages:
             continue
-        if name.startswith("tri_mul"):
+        if name == "transition":
+            _tr.forward(x4, pre["transition"], eps=eps, out=x4)
+        elif name.startswith("tri_mul"):
             residual_update(x4, pre[name], "outgoing" if name == "tri_mul_out" else "incoming", mask=m3, eps=eps)
         else:
             p = pre[name]
