@@ -8,11 +8,13 @@ namespace tops {
 
 template <typename T>
 int launch_zbias(const void* z, const ZBiasArgs& args, cudaStream_t st) {
-  const long long groups = (args.n_tok + 3) / 4;  // 4 tokens per warp iteration
-  long long blocks = (groups + 7) / 8;
-  const long long cap = static_cast<long long>(sm_count()) * 8;
-  if (blocks > cap) blocks = cap;
-  zbias_kernel<T, 128, 4><<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const T*>(z), args);
+  if (!aligned16(z)) return TOPS_ERR_ALIGN;
+  const long long tiles = (args.n_tok + kZbTile - 1) / kZbTile;
+  const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
+  const size_t smem = sizeof(ZbSmem) + 128;
+  auto kern = zbias_kernel<T, 128, 4>;
+  set_smem(kern, smem);
+  kern<<<grid, kZbThreads, smem, st>>>(static_cast<const T*>(z), args);
   return launch_status();
 }
 
