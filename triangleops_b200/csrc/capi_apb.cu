@@ -7,14 +7,15 @@
 namespace tops {
 
 template <typename T>
-int launch_zbias(const void* z, const ZBiasArgs& args, cudaStream_t st) {
-  if (!aligned16(z)) return TOPS_ERR_ALIGN;
+int launch_zbias(int dtype, const void* z, const ZBiasArgs& args, cudaStream_t st) {
+  CUtensorMap mz;
+  if (!map_rows(&mz, dtype, z, args.n_tok, 128, kZbTile)) return TOPS_ERR_TMAP;
   const long long tiles = (args.n_tok + kZbTile - 1) / kZbTile;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  const size_t smem = sizeof(ZbSmem) + 128;
+  const size_t smem = sizeof(ZbSmem) + 1024;
   auto kern = zbias_kernel<T, 128, 4>;
   set_smem(kern, smem);
-  kern<<<grid, kZbThreads, smem, st>>>(static_cast<const T*>(z), args);
+  kern<<<grid, kZbThreads, smem, st>>>(mz, args);
   return launch_status();
 }
 
@@ -38,7 +39,8 @@ extern "C" int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t M
   const int m = static_cast<int>(M), mq = static_cast<int>(Mq);
   const int mkp = (m + 7) & ~7;
   ZBiasArgs za{static_cast<long long>(Mq) * M, m, mkp, mq, eps, wc, sum_w, b_const, static_cast<__half*>(bias_ws)};
-  int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(z_rows, za, st) : launch_zbias<__half>(z_rows, za, st);
+  int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(dtype, z_rows, za, st)
+                              : launch_zbias<__half>(dtype, z_rows, za, st);
   if (rc != TOPS_OK) return rc;
   // Q/K/V projection of the whole (replicated, M x C) sequence: K/V are needed for
   // every key, and Q for all M rows costs less than a gather of the window; the

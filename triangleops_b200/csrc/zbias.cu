@@ -6,7 +6,8 @@
 // i.e. LN(z) W_proj_z + B_proj_z with the LN affine folded into (Wc, sumW, Bc)
 // [attn_pair_bias/module.py:29-35, attn_pair_bias/kernel.py:149-185]. The reference
 // recomputes this inside the attention loop once per head (z read H times); here
-// z streams through shared memory by bulk copies, eight lanes share one token (16-byte vector loads, 256 contiguous bytes per
+// z streams through shared memory by TMA, the tensor core takes the head dots and one
+// thread per token the statistics (16-byte vector loads, 256 contiguous bytes per
 // token), merge their partial statistics with warp-shuffle Welford (Chan's
 // pairwise update for equal counts) and reduce the H dot products in the same
 // shuffle tree. The logits are stored as f16 in log2 units, the operand format of the
@@ -27,133 +28,159 @@ struct ZBiasArgs {
   __half* bias;         // [H][Mq][Mkp] f16, in log2 units (times log2(e))
 };
 
-constexpr int kZbTile = 128;        // tokens per bulk copy (32 KB at Cz = 128, bf16)
-constexpr int kZbStages = 6;        // tiles in flight per SM
-constexpr int kZbWarps = 12;        // consumer warps
-constexpr int kZbThreads = 32 * (kZbWarps + 1);
+constexpr int kZbTile = 128;        // tokens per tile (one TMEM lane each)
+constexpr int kZbStages = 5;        // tiles in flight per SM (32 KB each)
+constexpr int kZbThreads = 256;     // w0 TMA, w1 MMA, w4..w7 statistics / epilogue
 
 struct ZbSmem {
-  alignas(128) uint8_t tile[kZbStages][kZbTile * 256];
+  alignas(1024) uint8_t tile[kZbStages][2][16384];  // z tile: 128 tokens x 128 ch, two SW128 atoms
+  alignas(1024) uint8_t wt[2][2048];                // B: 16 rows (W_hi | W_lo | 0) x 128 ch, two atoms
   uint64_t full[kZbStages], empty[kZbStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
   int abort;
 };
 
-// Persistent, one CTA per SM: warp kZbWarps streams contiguous 128-token tiles of z into
-// a kZbStages-deep shared-memory ring with bulk copies (so the bytes in flight per SM do
-// not depend on how many threads the math leaves room for), and kZbWarps warps reduce
-// them: eight lanes per token, each lane two 16-byte chunks (channels [8s, 8s+8) and
-// [64+8s, 64+8s+8)), read conflict-free from shared memory.
+// Persistent, one CTA per SM. The per-head dot products z . Wc[h] run on the tensor core:
+// D[token, n] = sum_c z[token, c] B[n, c] with B rows 0..3 = Wc rounded to the IO dtype
+// and rows 4..7 = the rounding residue (so D[h] + D[4+h] carries the fp32 weights), one
+// M=128, N=16, K=128 MMA chain per 128-token tile. The LayerNorm statistics need the
+// second moment, which is not linear in z: one thread per token computes mean and
+// variance (two passes over its row in registers) from the same shared-memory tile,
+// then combines them with the dots and stores the four heads' logits (consecutive
+// threads write consecutive keys).
 template <typename T, int CZ, int H>
-__global__ void __launch_bounds__(kZbThreads, 1) zbias_kernel(const T* __restrict__ z, ZBiasArgs a) {
+__global__ void __launch_bounds__(kZbThreads, 1)
+    zbias_kernel(const __grid_constant__ CUtensorMap map_z, ZBiasArgs a) {
   using E = Elem<T>;
-  static_assert(CZ == 128, "one token = 8 lanes x 16 channels = 256 bytes");
+  static_assert(CZ == 128 && H == 4, "Cz = 128, four heads");
   extern __shared__ uint8_t smem_raw[];
-  ZbSmem& sm = *reinterpret_cast<ZbSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+  ZbSmem& sm = *reinterpret_cast<ZbSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long n_tiles = (a.n_tok + kZbTile - 1) / kZbTile;
+  // B tile: element (n, c) of the K-major SW128 layout at atom c/64, n*128 + ((c%64/8 ^ n%8)*16) + (c%8)*2
+  for (int idx = threadIdx.x; idx < 16 * CZ; idx += blockDim.x) {
+    const int n = idx / CZ, c = idx % CZ;
+    float v = 0.f;
+    if (n < H) {
+      v = a.wc[n * CZ + c];
+    } else if (n < 2 * H) {
+      const float w = a.wc[(n - H) * CZ + c];
+      v = w - E::to_f(E::from_f(w));
+    }
+    const T tv = E::from_f(v);
+    *reinterpret_cast<T*>(sm.wt[c >> 6] + n * 128 + ((((c & 63) >> 3) ^ (n & 7)) << 4) + (c & 7) * 2) = tv;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kZbStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kZbWarps);
+      mbar_init(&sm.empty[s], 1 + 4);  // the MMA commit and the four statistics warps
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);
     }
     sm.abort = 0;
     fence_mbar_init();
   }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, 32);
+  fence_proxy_async_smem();
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
   volatile int* abort = &sm.abort;
-  if (warp == kZbWarps) {
+
+  if (warp == 0) {
     if (lane == 0) {
+      tma_prefetch_desc(&map_z);
       int it = 0;
       for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
         const int s = it % kZbStages;
         if (!mbar_wait(&sm.empty[s], ((it / kZbStages) & 1) ^ 1, abort, 601)) break;
-        const long long t0 = t * kZbTile;
-        const long long n = a.n_tok - t0 < kZbTile ? a.n_tok - t0 : kZbTile;
-        const uint32_t bytes = static_cast<uint32_t>(n) * CZ * 2;
-        mbar_expect_tx(&sm.full[s], bytes);
-        bulk_load(sm.tile[s], z + t0 * CZ, bytes, &sm.full[s]);
+        mbar_expect_tx(&sm.full[s], 2 * 16384);
+        tma_load_2d(sm.tile[s][0], &map_z, &sm.full[s], 0, static_cast<int>(t * kZbTile));
+        tma_load_2d(sm.tile[s][1], &map_z, &sm.full[s], 64, static_cast<int>(t * kZbTile));
       }
     }
-    return;
-  }
-  // this lane's channels: [sub*8, sub*8+8) and [64+sub*8, 64+sub*8+8)
-  float w[H][16];
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, 16, E::kFmt, false, false);
+      int it = 0;
+      for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+        const int s = it % kZbStages, b = it & 1;
+        if (!mbar_wait(&sm.full[s], (it / kZbStages) & 1, abort, 602)) break;
+        if (it >= 2 && !mbar_wait(&sm.acc_empty[b], ((it >> 1) - 1) & 1, abort, 603)) break;
+        tc_fence_after();
 #pragma unroll
-  for (int h = 0; h < H; ++h)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      w[h][e] = a.wc[h * CZ + sub * 8 + e];
-      w[h][8 + e] = a.wc[h * CZ + 64 + sub * 8 + e];
-    }
-  float sw[H], bc[H];
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    sw[h] = a.sum_w[h];
-    bc[h] = a.b_const[h];
-  }
-  int it = 0;
-  for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-    const int s = it % kZbStages;
-    if (!mbar_wait(&sm.full[s], (it / kZbStages) & 1, abort, 602)) break;
-    for (int gi = warp; gi < kZbTile / 4; gi += kZbWarps) {
-      const int local = gi * 4 + grp;
-      const long long tok = t * kZbTile + local;
-      const bool valid = tok < a.n_tok;
-      const uint4* src = reinterpret_cast<const uint4*>(sm.tile[s] + local * 256);
-      const uint4 u0 = src[sub], u1 = src[8 + sub];
-      float v[16];
-      {
-        const uint32_t p[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          v[2 * e] = E::lo(p[e]);
-          v[2 * e + 1] = E::hi(p[e]);
-        }
+        for (int kk = 0; kk < CZ / 16; ++kk)
+          mma_ss(tbase + b * 16, make_smem_desc(smem_u32(sm.tile[s][kk >> 2]) + (kk & 3) * 32, 16, 1024, kSw128),
+                 make_smem_desc(smem_u32(sm.wt[kk >> 2]) + (kk & 3) * 32, 16, 1024, kSw128), idesc, kk > 0);
+        mma_commit(&sm.acc_full[b]);
+        mma_commit(&sm.empty[s]);
       }
-      float mean = 0.f;
+    }
+  } else if (warp >= 4) {
+    const int wq = warp & 3, r = wq * 32 + lane;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
+    float sw[H], bc[H];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) mean += v[e];
-      mean *= (1.0f / 16);
+    for (int h = 0; h < H; ++h) {
+      sw[h] = a.sum_w[h];
+      bc[h] = a.b_const[h];
+    }
+    int it = 0;
+    for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      const int s = it % kZbStages, b = it & 1;
+      if (!mbar_wait(&sm.full[s], (it / kZbStages) & 1, abort, 604)) break;
+      uint32_t p[64];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sm.tile[s][c >> 3] + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
+        p[4 * c] = u.x;
+        p[4 * c + 1] = u.y;
+        p[4 * c + 2] = u.z;
+        p[4 * c + 3] = u.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[s]);
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) sum += E::lo(p[e]) + E::hi(p[e]);
+      const float mean = sum * (1.0f / CZ);
       float m2 = 0.f;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float d = v[e] - mean;
-        m2 = fmaf(d, d, m2);
-      }
-      float dot[H];
-#pragma unroll
-      for (int h = 0; h < H; ++h) {
-        float acc = 0.f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) acc = fmaf(v[e], w[h][e], acc);
-        dot[h] = acc;
-      }
-      // merge the 8 lanes of a token: Welford/Chan for equal counts, and the dots
-      float n = 16.f;
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) {
-        const float om = __shfl_xor_sync(0xffffffffu, mean, off);
-        const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
-        const float d = om - mean;
-        mean += 0.5f * d;
-        m2 += o2 + d * d * (0.5f * n);
-        n *= 2.f;
-#pragma unroll
-        for (int h = 0; h < H; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
+      for (int e = 0; e < 64; ++e) {
+        const float d0 = E::lo(p[e]) - mean, d1 = E::hi(p[e]) - mean;
+        m2 = fmaf(d0, d0, fmaf(d1, d1, m2));
       }
       const float rstd = rsqrtf(m2 * (1.0f / CZ) + a.eps);
-      if (valid && sub < H) {
-        float bv = 0.f;
-#pragma unroll
-        for (int h = 0; h < H; ++h)
-          if (h == sub) bv = fmaf(rstd, dot[h] - mean * sw[h], bc[h]);
+      if (!mbar_wait(&sm.acc_full[b], (it >> 1) & 1, abort, 605)) break;
+      tc_fence_after();
+      uint32_t d[8];
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+                   "tcgen05.wait::ld.sync.aligned;"
+                   : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7])
+                   : "r"(lane_addr + b * 16)
+                   : "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      const long long tok = t * kZbTile + r;
+      if (tok < a.n_tok) {
         const long long q = tok / a.M, k = tok - q * a.M;
-        a.bias[(static_cast<long long>(sub) * a.Mq + q) * a.Mkp + k] = __float2half_rn(bv * 1.4426950408889634f);
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          const float dot = __uint_as_float(d[h]) + __uint_as_float(d[H + h]);
+          const float bv = fmaf(rstd, dot - mean * sw[h], bc[h]);
+          a.bias[(static_cast<long long>(h) * a.Mq + q) * a.Mkp + k] = __float2half_rn(bv * 1.4426950408889634f);
+        }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s]);
   }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 32);
 }
 
 }  // namespace tops
