@@ -600,29 +600,34 @@ def main():
         barrier()
         return e0.elapsed_time(e1) / iters
 
-    e2e_iters = max(3, min(args.steps, 5))
-    # single-call latency: one call at a time, each waited for
-    lat = []
-    for _ in range(e2e_iters + 1):
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        e2e_step()
-        e1.record(stream)
-        barrier()
-        lat.append(e0.elapsed_time(e1))
-    e2e_latency_ms = sorted(lat[1:])[len(lat[1:]) // 2]
-    e2e_serial_ms = timed(e2e_step, e2e_iters)
+    e2e_iters = max(5, min(args.steps, 20))
+    # serial: H2D, forward, D2H, one call after another
+    e2e_serial_ms = timed(e2e_step, min(e2e_iters, 5))
     e2e_ms, e2e_method = e2e_serial_ms, "serial: H2D, forward, D2H per call, back to back"
+    call, fin = e2e_step, None
     if n % 8 == 0:
         # the host-tensor API: row slabs stream in and out on copy streams, and the copies of
         # consecutive calls overlap (PCIe is full duplex); with P ranks each pipes its own
         # rows and the bias rows are all-gathered between the two stages
         pipe = tops.triangle_attn.HostPipeline(pre, W_proj_g=inp["W_proj_g"], W_proj_o=inp["W_proj_o"],
                                                scale=scale)
-        e2e_ms = timed(lambda: pipe(X_h, m_h, out_h), e2e_iters, finish=pipe.wait)
-        e2e_method = ("triangle_attn.HostPipeline, calls back to back (throughput): slab-streamed H2D/D2H "
-                      "overlapping compute and consecutive calls")
+        call, fin = (lambda: pipe(X_h, m_h, out_h)), pipe.wait
+        e2e_ms = timed(call, e2e_iters, finish=fin)
+        e2e_method = (f"triangle_attn.HostPipeline, {e2e_iters} calls back to back (throughput, including one "
+                      "pipeline fill and drain): slab-streamed H2D/D2H overlapping compute and consecutive calls")
+    # single-call latency through the same call: one call at a time, each waited for
+    lat = []
+    for _ in range(4):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call()
+        if fin is not None:
+            fin()
+        e1.record(stream)
+        barrier()
+        lat.append(e0.elapsed_time(e1))
+    e2e_latency_ms = sorted(lat[1:])[len(lat[1:]) // 2]
 
     if world > 1:
         t = torch.tensor([ms, attn_ms, e2e_ms, e2e_latency_ms, e2e_serial_ms], device=dev)
