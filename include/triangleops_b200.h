@@ -230,7 +230,7 @@ int tops_f32_layernorm(int64_t T, int64_t C, const float* x, const float* w, con
 int tops_f32_gemm(int64_t batch, int64_t M, int64_t N, int64_t K, const float* A, const float* B, const float* bias,
                   float* C, const int64_t* strides, void* stream);
 
-/* O[r][q][h*D+d] = softmax_k(scale * q.k + bias[h][q][k]) v, D in {16, 32}.
+/* O[r][q][h*D+d] = softmax_k(scale * q.k + bias[h][q][k]) v, 1 <= D <= 128.
  * q/k/v element (r,h,n,d) at r*sr + h*sh + n*sn + d; mask [R][Nk] uint8 or NULL;
  * mask_mode 0: masked keys get -1e9 added (triangle attention); 1: masked keys dropped. */
 int tops_f32_attention(int64_t R, int64_t H, int64_t Nq, int64_t Nk, int64_t D, const float* q, const float* k,

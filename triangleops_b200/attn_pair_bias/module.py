@@ -47,6 +47,12 @@ def forward(X, Z, pre, *, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_proj_o, B_p
         WQ, WK, WV, W_ln, B_ln, W_pz, B_pz = pre["f32"]
         return _f32.attention_pair_bias(X, WQ, WK, WV, Z, W_ln, B_ln, W_pz, B_pz, W_proj_g, B_proj_g, W_proj_o,
                                         B_proj_o, H, D, scale, eps, mask)
+    if (X.shape[-1], Z.shape[-1], H, D) != (128, 128, 4, 32):
+        # the tcgen05 path is built for c_s = C_z = 128, H = 4, D = 32; other shapes run on
+        # the CUDA-core fp32 kernels and round back once
+        WQ, WK, WV, W_ln, B_ln, W_pz, B_pz = pre["f32"]
+        return _f32.attention_pair_bias(X.float(), WQ, WK, WV, Z.float(), W_ln, B_ln, W_pz, B_pz, W_proj_g, B_proj_g,
+                                        W_proj_o, B_proj_o, H, D, scale, eps, mask).to(X.dtype)
     w = pre["w_rows"]
     if w.dtype != X.dtype:
         w = w.to(X.dtype)

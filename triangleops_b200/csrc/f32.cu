@@ -93,40 +93,43 @@ __global__ void __launch_bounds__(256) f32_gemm_kernel(const float* __restrict__
 // mask [R][Nk] uint8 or null. mask_mode 0: masked keys get -1e9 added (triangle attention,
 // triangle_attn/kernel.py:233-238); mask_mode 1: masked keys are dropped (-inf,
 // benchmarks/references.py:273-274). S = scale * (q . k) + bias. O: [R][Nq][H*D].
-template <int D>
+// Head size D <= DMAX at run time (registers and shared tiles sized by DMAX; KB keys per
+// shared-memory block).
+template <int DMAX, int KB>
 __global__ void __launch_bounds__(128) f32_attn_kernel(const float* __restrict__ Q, const float* __restrict__ K,
                                                        const float* __restrict__ V, const float* __restrict__ bias,
                                                        const unsigned char* __restrict__ mask, float* __restrict__ O,
                                                        int R, int H, int Nq, int Nk, float scale, int mask_mode,
-                                                       long long sr, long long sh, long long sn) {
-  __shared__ float Ks[64][D + 1];
-  __shared__ float Vs[64][D + 1];
+                                                       long long sr, long long sh, long long sn, int D) {
+  __shared__ float Ks[KB][DMAX + 1];
+  __shared__ float Vs[KB][DMAX + 1];
   const int r = blockIdx.z, h = blockIdx.y;
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   const bool qv = q < Nq;
-  float qr[D], o[D];
+  float qr[DMAX], o[DMAX];
   const float* qp = Q + r * sr + h * sh + static_cast<long long>(qv ? q : 0) * sn;
 #pragma unroll
-  for (int d = 0; d < D; ++d) {
-    qr[d] = qp[d];
+  for (int d = 0; d < DMAX; ++d) {
+    qr[d] = d < D ? qp[d] : 0.f;
     o[d] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
   const float* kb = K + r * sr + h * sh;
   const float* vb = V + r * sr + h * sh;
-  for (int k0 = 0; k0 < Nk; k0 += 64) {
-    for (int i = threadIdx.x; i < 64 * D; i += blockDim.x) {
+  for (int k0 = 0; k0 < Nk; k0 += KB) {
+    for (int i = threadIdx.x; i < KB * D; i += blockDim.x) {
       const int kk = i / D, d = i % D;
       Ks[kk][d] = k0 + kk < Nk ? kb[static_cast<long long>(k0 + kk) * sn + d] : 0.f;
       Vs[kk][d] = k0 + kk < Nk ? vb[static_cast<long long>(k0 + kk) * sn + d] : 0.f;
     }
     __syncthreads();
-    const int kn = Nk - k0 < 64 ? Nk - k0 : 64;
+    const int kn = Nk - k0 < KB ? Nk - k0 : KB;
     for (int kk = 0; kk < kn; ++kk) {
       const int k = k0 + kk;
       float sdot = 0.f;
 #pragma unroll
-      for (int d = 0; d < D; ++d) sdot = fmaf(qr[d], Ks[kk][d], sdot);
+      for (int d = 0; d < DMAX; ++d)
+        if (d < D) sdot = fmaf(qr[d], Ks[kk][d], sdot);
       float sv = scale * sdot + (qv ? bias[(static_cast<long long>(h) * Nq + q) * Nk + k] : 0.f);
       if (mask != nullptr && !mask[static_cast<long long>(r) * Nk + k]) {
         if (mask_mode == 1) continue;
@@ -136,7 +139,8 @@ __global__ void __launch_bounds__(128) f32_attn_kernel(const float* __restrict__
       const float alpha = expf(m - mn), p = expf(sv - mn);
       l = l * alpha + p;
 #pragma unroll
-      for (int d = 0; d < D; ++d) o[d] = fmaf(o[d], alpha, p * Vs[kk][d]);
+      for (int d = 0; d < DMAX; ++d)
+        if (d < D) o[d] = fmaf(o[d], alpha, p * Vs[kk][d]);
       m = mn;
     }
     __syncthreads();
@@ -145,7 +149,8 @@ __global__ void __launch_bounds__(128) f32_attn_kernel(const float* __restrict__
     float* op = O + (static_cast<long long>(r) * Nq + q) * (H * D) + h * D;
     const float inv = 1.f / l;
 #pragma unroll
-    for (int d = 0; d < D; ++d) op[d] = o[d] * inv;
+    for (int d = 0; d < DMAX; ++d)
+      if (d < D) op[d] = o[d] * inv;
   }
 }
 
@@ -197,14 +202,22 @@ extern "C" int tops_f32_attention(int64_t R, int64_t H, int64_t Nq, int64_t Nk, 
   if (mask_mode != 0 && mask_mode != 1) return TOPS_ERR_ARG;
   dim3 grid(static_cast<unsigned>((Nq + 127) / 128), static_cast<unsigned>(H), static_cast<unsigned>(R));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (D == 32)
-    f32_attn_kernel<32><<<grid, 128, 0, st>>>(q, k, v, bias, mask, out, static_cast<int>(R), static_cast<int>(H),
-                                             static_cast<int>(Nq), static_cast<int>(Nk), scale, mask_mode, sr, sh, sn);
-  else if (D == 16)
-    f32_attn_kernel<16><<<grid, 128, 0, st>>>(q, k, v, bias, mask, out, static_cast<int>(R), static_cast<int>(H),
-                                             static_cast<int>(Nq), static_cast<int>(Nk), scale, mask_mode, sr, sh, sn);
-  else
+  const int d = static_cast<int>(D);
+#define TOPS_F32_ATTN(DM, KB)                                                                                     \
+  f32_attn_kernel<DM, KB><<<grid, 128, 0, st>>>(q, k, v, bias, mask, out, static_cast<int>(R), static_cast<int>(H), \
+                                                static_cast<int>(Nq), static_cast<int>(Nk), scale, mask_mode, sr, sh, \
+                                                sn, d)
+  if (D <= 0 || D > 128)
     return TOPS_ERR_SHAPE;
+  else if (D <= 16)
+    TOPS_F32_ATTN(16, 64);
+  else if (D <= 32)
+    TOPS_F32_ATTN(32, 64);
+  else if (D <= 64)
+    TOPS_F32_ATTN(64, 64);
+  else
+    TOPS_F32_ATTN(128, 32);
+#undef TOPS_F32_ATTN
   return cudaGetLastError() == cudaSuccess ? TOPS_OK : TOPS_ERR_CUDA;
 }
 

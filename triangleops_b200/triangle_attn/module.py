@@ -17,6 +17,10 @@ from .._common.layouts import interleave_kv, qkv_rows
 from .kernel import attend_rows, gate_forward, is_transposed_rows, project_rows, triangle_attn_fused_forward
 
 
+# (C, H, D) the tensor-core kernels are built for; any other C = H*D runs on the fp32 kernels
+TENSOR_CORE_SHAPES = ((128, 4, 32), (64, 4, 16))
+
+
 def precompute(W_ln, B_ln, WQ, WK, WV, W_proj_z, B_proj_z, H, D):
     """One-time layout prep (``module.py:19-50``). WQ/WK/WV are (C, H*D) and
     W_proj_z (C, H) (matmul convention). Returns an opaque dict for ``forward``."""
@@ -57,8 +61,14 @@ def forward(X, pre, *, mask=None, scale=1.0, eps=1e-5, W_proj_g, B_proj_g, W_pro
     )
     H, D = pre["H"], pre["D"]
     N = X.shape[0]
+    C = X.shape[-1]
     if X.dtype == torch.float32:
         return _f32.triangle_attention(X, *pre["f32"], W_proj_g, W_proj_o, H, D, scale, eps, mask)
+    if (C, H, D) not in TENSOR_CORE_SHAPES:
+        # the reference takes any C = H*D; the tcgen05 kernels are built for the shapes
+        # above, so other shapes run on the CUDA-core fp32 kernels and round back once
+        return _f32.triangle_attention(X.float(), *pre["f32"], W_proj_g, W_proj_o, H, D, scale, eps,
+                                       mask).to(X.dtype)
     w = pre["W_qkvz"]
     if w.dtype != X.dtype:
         w = w.to(X.dtype)

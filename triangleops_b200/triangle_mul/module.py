@@ -60,6 +60,10 @@ def forward(x, pre, *, direction, mask=None, eps=1e-5):
     B, L, _, C = x.shape
     if x.dtype == torch.float32:
         return _f32.triangle_multiplicative_update(x, pre["f32"], direction, mask, eps)
+    if C not in (64, 128):
+        # the tcgen05 kernels are built for C = 64 and 128; other widths run on the
+        # CUDA-core fp32 kernels and round back once
+        return _f32.triangle_multiplicative_update(x.float(), pre["f32"], direction, mask, eps).to(x.dtype)
     Lp = (L + 7) // 8 * 8
     if Lp == L:
         return fused_forward(x, pre, direction, mask=mask, eps=eps)
