@@ -10,7 +10,8 @@
 // Persistent kernel, one 128-token tile at a time per CTA, the hidden dimension in
 // chunks of 64:
 //   w0       TMA producer: per chunk h the weight stage [W1'_h ; W2'_h] (128 x C) and
-//            W3_h (C x 64) into a 3-deep ring
+//            W3_h (C x 64) into a 2-deep ring
+//   w3       TMA producer of the x tiles (the next tile's x lands during this tile's chunks)
 //   w1       MMA1 issuer: U_h = xhat [W1'_h ; W2'_h]^T (N = 128: u | v) into one of two
 //            TMEM buffers
 //   w2       MMA2 issuer: ACC += H_h W3_h^T (N = C)
@@ -27,15 +28,18 @@ constexpr int kTrC = 128;            // channels
 constexpr int kTrNH = 4 * kTrC;      // hidden width
 constexpr int kTrCH = 64;            // hidden chunk
 constexpr int kTrNCH = kTrNH / kTrCH;  // chunks per tile
-constexpr int kTrStages = 3;
+constexpr int kTrStages = 2;
 constexpr int kTrWG = 2;              // LayerNorm / SwiGLU / epilogue warpgroups (column halves)
 constexpr int kTrThreads = 128 + 128 * kTrWG;
 
 struct TrSmem {
+  alignas(1024) uint8_t xraw[2][16384];          // x tile as loaded: 128 rows x 128 ch, two SW128 atoms
   alignas(1024) uint8_t xh[2][16384];            // xhat tile: 128 rows x 128 ch, two 64-ch SW128 atoms
   alignas(1024) uint8_t hbuf[2][16384];          // H_h: 128 rows x 64 hidden, one SW128 atom, two buffers
   alignas(1024) uint8_t w12[kTrStages][2][16384];  // [W1'_h ; W2'_h]: 128 rows x 128 K (two K atoms)
   alignas(1024) uint8_t w3[kTrStages][16384];    // W3_h: 128 rows (C) x 64 K (hidden)
+  float b12[kTrNCH * 128];                       // the folded biases of every chunk
+  uint64_t x_full, x_empty;                      // x tile landed / every warpgroup has read it
   uint64_t w_full[kTrStages], w_empty[kTrStages];
   uint64_t xh_full, xh_empty;                    // xhat written / every MMA1 of the tile done
   uint64_t u_full[2], u_empty[2];                // U buffer b holds chunk h / was read
@@ -60,14 +64,17 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 
 template <typename T>
 __global__ void __launch_bounds__(kTrThreads, 1)
-    transition_kernel(const __grid_constant__ CUtensorMap map_w12, const __grid_constant__ CUtensorMap map_w3,
-                      TrArgs a) {
+    transition_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w12,
+                      const __grid_constant__ CUtensorMap map_w3, TrArgs a) {
   using E = Elem<T>;
   extern __shared__ uint8_t smem_raw[];
   TrSmem& sm = *reinterpret_cast<TrSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (a.M + 127) / 128;
+  for (int i = threadIdx.x; i < kTrNCH * 128; i += blockDim.x) sm.b12[i] = a.b12[i];
   if (threadIdx.x == 0) {
+    mbar_init(&sm.x_full, 1);
+    mbar_init(&sm.x_empty, 4 * kTrWG);
     for (int s = 0; s < kTrStages; ++s) {
       mbar_init(&sm.w_full[s], 1);
       mbar_init(&sm.w_empty[s], 2);  // MMA1 (W12) and MMA2 (W3) both release the stage
@@ -109,6 +116,18 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           tma_load_2d(sm.w12[s][1], &map_w12, &sm.w_full[s], 64, h * 128);
           tma_load_2d(sm.w3[s], &map_w3, &sm.w_full[s], h * kTrCH, 0);
         }
+      }
+    }
+  } else if (warp == 3) {
+    if (lane == 0) {
+      // ---------------- x tiles: the next tile's x lands while this tile computes ----------------
+      tma_prefetch_desc(&map_x);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        if (!mbar_wait(&sm.x_empty, (it & 1) ^ 1, abort, 812)) break;
+        mbar_expect_tx(&sm.x_full, 2 * 16384);
+        tma_load_2d(sm.xraw[0], &map_x, &sm.x_full, 0, tile * 128);
+        tma_load_2d(sm.xraw[1], &map_x, &sm.x_full, 64, tile * 128);
       }
     }
   } else if (warp == 1) {
@@ -171,20 +190,21 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     const int wq = warp & 3, k = (warp - 4) >> 2;
     const int row = wq * 32 + lane;  // token row of the tile == TMEM lane
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint4* xg = static_cast<const uint4*>(a.x);
     int g = 0, it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int tok = tile * 128 + row;
       const bool valid = tok < a.M;
-      // LayerNorm statistics of the whole row (fp32); this warpgroup writes its QX columns
-      uint4 xv[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) xv[c] = valid ? xg[static_cast<size_t>(tok) * 16 + c] : make_uint4(0, 0, 0, 0);
+      // LayerNorm statistics of the whole row (fp32) from the staged x tile; this warpgroup
+      // writes its QX columns of xhat and keeps them of x for the residual
+      if (!mbar_wait(&sm.x_full, it & 1, abort, 813)) { ok = false; break; }
+      // two streaming passes over the row in shared memory (few live registers)
+      auto xchunk = [&](int c) { return *reinterpret_cast<const uint4*>(sm.xraw[c >> 3] + sw128_off(row, (c & 7) * 8)); };
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+        const uint4 v4 = xchunk(c);
+        const uint32_t w4[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) sum += E::lo(w4[e]) + E::hi(w4[e]);
       }
@@ -192,7 +212,8 @@ __global__ void __launch_bounds__(kTrThreads, 1)
       float var = 0.f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+        const uint4 v4 = xchunk(c);
+        const uint32_t w4[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float d0 = E::lo(w4[e]) - mean, d1 = E::hi(w4[e]) - mean;
@@ -200,16 +221,22 @@ __global__ void __launch_bounds__(kTrThreads, 1)
         }
       }
       const float rstd = valid ? rsqrtf(var * (1.0f / kTrC) + a.eps) : 0.f;
+      // this warpgroup's columns of x: the residual and the xhat it writes
+      uint4 xres[QX / 8];
+#pragma unroll
+      for (int c = 0; c < QX / 8; ++c) xres[c] = xchunk(k * (QX / 8) + c);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.x_empty);
       // the previous tile's MMA1s must be done with the xhat tile
       if (it > 0 && !mbar_wait(&sm.xh_empty, (it - 1) & 1, abort, 808)) { ok = false; break; }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        if (c / (QX / 8) != k) continue;  // 8-column chunks of this warpgroup's quarter
-        const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+      for (int c = 0; c < QX / 8; ++c) {
+        const uint32_t w4[4] = {xres[c].x, xres[c].y, xres[c].z, xres[c].w};
         uint32_t o4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) o4[e] = E::pack2((E::lo(w4[e]) - mean) * rstd, (E::hi(w4[e]) - mean) * rstd);
-        *reinterpret_cast<uint4*>(sm.xh[c >> 3] + sw128_off(row, (c & 7) * 8)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+        const int cg = k * (QX / 8) + c;  // 8-column chunk of the row
+        *reinterpret_cast<uint4*>(sm.xh[cg >> 3] + sw128_off(row, (cg & 7) * 8)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&sm.xh_full);
@@ -222,7 +249,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           tmem_ld16x2_async(lane_addr + ub * 128 + k * QH, lane_addr + ub * 128 + 64 + k * QH, uv);
           tmem_wait_ld32(uv);
         } else {
-          static_assert(QH == 32, "u and v loads of 16 or 32 columns");
+          static_assert(QH == 32 || QH == 16, "u and v loads of 16 or 32 columns");
           tmem_ld32(lane_addr + ub * 128 + k * QH, uv);
           tmem_ld32(lane_addr + ub * 128 + 64 + k * QH, uv + QH);
         }
@@ -230,11 +257,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
         const uint32_t* v = uv + QH;
         tc_fence_before();
         mbar_arrive(&sm.u_empty[ub]);
-        const float4* bb = reinterpret_cast<const float4*>(a.b12 + h * 128 + k * QH);
+        const float4* bb = reinterpret_cast<const float4*>(sm.b12 + h * 128 + k * QH);
         uint32_t hp[QH / 2];
 #pragma unroll
         for (int c = 0; c < QH / 4; ++c) {
-          const float4 b1 = __ldg(bb + c), b2 = __ldg(bb + 16 + c);
+          const float4 b1 = bb[c], b2 = bb[16 + c];
           const float u0 = __uint_as_float(u[4 * c]) + b1.x, u1 = __uint_as_float(u[4 * c + 1]) + b1.y;
           const float u2 = __uint_as_float(u[4 * c + 2]) + b1.z, u3 = __uint_as_float(u[4 * c + 3]) + b1.w;
           const float v0 = __uint_as_float(v[4 * c]) + b2.x, v1 = __uint_as_float(v[4 * c + 1]) + b2.y;
@@ -261,12 +288,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
       tc_fence_before();
       mbar_arrive(&sm.acc_empty);
       if (valid) {
-        const uint4* xr = xg + static_cast<size_t>(tok) * 16 + k * QX / 8;
         uint4* dst = static_cast<uint4*>(a.out) + static_cast<size_t>(tok) * 16 + k * QX / 8;
         static_assert(QX % 32 == 0, "epilogue in 32-column loads");
 #pragma unroll
         for (int q = 0; q < QX / 8; ++q) {
-          const uint4 xq = xr[q];
+          const uint4 xq = xres[q];
           const uint32_t w4[4] = {xq.x, xq.y, xq.z, xq.w};
           uint32_t o4[4];
 #pragma unroll
@@ -291,7 +317,8 @@ namespace tops {
 template <typename T>
 int launch_transition(int dtype, int64_t M, const void* x, const void* w12, const void* w3, const float* b12,
                       float eps, void* out, cudaStream_t st) {
-  CUtensorMap m12, m3;
+  CUtensorMap mx, m12, m3;
+  if (!map_rows(&mx, dtype, x, M, kTrC, 128)) return TOPS_ERR_TMAP;
   if (!map_rows(&m12, dtype, w12, kTrNH * 2, kTrC, 128)) return TOPS_ERR_TMAP;
   if (!map_rows(&m3, dtype, w3, kTrC, kTrNH, 128)) return TOPS_ERR_TMAP;
   TrArgs args{static_cast<int>(M), eps, x, out, b12};
@@ -300,7 +327,7 @@ int launch_transition(int dtype, int64_t M, const void* x, const void* w12, cons
   set_smem(kern, smem);
   const long long tiles = (M + 127) / 128;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, kTrThreads, smem, st>>>(m12, m3, args);
+  kern<<<grid, kTrThreads, smem, st>>>(mx, m12, m3, args);
   return launch_status();
 }
 }  // namespace tops
