@@ -410,9 +410,16 @@ def sharded_ops(dev, world, rank):
     x, mask, w = config3_inputs(dev)
     pre = tops.triangle_mul.precompute(*w)
     L = x.shape[1]
-    ms = time_op(lambda: tdist.triangle_multiplicative_update_rows(x, pre, direction="incoming", mask=mask), iters=10)
-    out["triangle_multiplicative_update"] = {"config": f"incoming L={L} C=128 bf16, mask tail 1900, row slabs x{world}",
-                                             "ms": tmax(ms), "tflops": 3.02e12 / tmax(ms) / 1e9}
+    tm = {}
+    for split in ("channels", "rows"):
+        ms = time_op(lambda: tdist.triangle_multiplicative_update_rows(x, pre, direction="incoming", mask=mask,
+                                                                        split=split), iters=10)
+        tm[split] = tmax(ms)
+    out["triangle_multiplicative_update"] = {
+        "config": f"incoming L={L} C=128 bf16, mask tail 1900, x replicated on {world} ranks, output rows sharded",
+        "ms": tm["channels"], "tflops": 3.02e12 / tm["channels"] / 1e9,
+        "split": "channels: input phase on all tokens, C/P channel planes contracted, one all-to-all of y",
+        "ms_rows_split": tm["rows"]}
     del x, mask
     params, xc = chain_inputs(dev)
     N = xc.shape[0]

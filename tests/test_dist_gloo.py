@@ -91,6 +91,12 @@ class CpuTrimulOps:
     COL_TILE = 1  # exercise the chunk-by-chunk exchange on CPU
 
     @staticmethod
+    def contract(a, b, direction):  # (D, B, L, L) planes
+        if direction == "outgoing":
+            return torch.einsum("dbik,dbjk->dbij", a, b)
+        return torch.einsum("dbki,dbkj->dbij", a, b)
+
+    @staticmethod
     def contract_cols(a, b_flat, direction, Mi, L, P, j0, jc, y):
         C, nc = a.shape[0], L // P
         ch = b_flat[j0 // nc]  # one chunk: (C, nc, L) outgoing / (C, L, nc) incoming
@@ -119,12 +125,13 @@ def _trimul_inputs(L=12):
     return r(1, L, L, C), (torch.rand(1, L, L, generator=g) > 0.2), w
 
 
-def _trimul_worker(rank, world, port, q, direction):
+def _trimul_worker(rank, world, port, q, direction, split):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         x, mask, w = _trimul_inputs()
-        out = tdist.triangle_multiplicative_update_rows(x, {"w": w}, direction=direction, mask=mask, ops=CpuTrimulOps)
+        out = tdist.triangle_multiplicative_update_rows(x, {"w": w}, direction=direction, mask=mask, ops=CpuTrimulOps,
+                                                        split=split)
         full = tdist.all_gather_rows(out[0].contiguous(), 0)
         if rank == 0:
             q.put(full)
@@ -132,15 +139,16 @@ def _trimul_worker(rank, world, port, q, direction):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("split,world", [("rows", 2), ("rows", 3), ("channels", 2), ("channels", 4)])
 @pytest.mark.parametrize("direction", ["outgoing", "incoming"])
-def test_sharded_triangle_mul_gloo(direction, world):
+def test_sharded_triangle_mul_gloo(direction, world, split):
     """Row slabs with b exchanged chunk by chunk (each peer's chunk contracted as it
-    arrives); 3 ranks exercise steps that pair every rank with two different peers."""
+    arrives; 3 ranks pair every rank with two different peers), and channel planes with
+    one all-to-all of y."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_trimul_worker, args=(r, world, port, q, direction)) for r in range(world)]
+    procs = [ctx.Process(target=_trimul_worker, args=(r, world, port, q, direction, split)) for r in range(world)]
     for p in procs:
         p.start()
     full = q.get(timeout=120)

@@ -10,11 +10,13 @@ only where the algorithm exchanges data:
   the gate run on local rows. Per rank the exchange is H*N*N*(P-1)/P elements
   (29 MB at N=2048, P=8).
 * triangle multiplicative update (x replicated, as in the 1/2/4/8-GPU configuration):
-  output row i needs a[., i, .] (outgoing: row i of a; incoming: column i of a) and
-  ALL of b. Each rank runs the input phase on the token slab that yields its a and
-  its share of b (outgoing: pair rows of the slab; incoming: pair columns), b is
-  all-gathered (C*L*L*(P-1)/P elements per rank), then the row-slab contraction
-  reads the gathered chunks in place and the output phase runs on the rank's rows.
+  by channel: the contraction is independent per channel d, so each rank contracts
+  C/P channel planes after an input phase over all tokens, and one all-to-all hands
+  every rank y of its rows (C*L*L/P^2 elements per peer). By rows (the chain, where x
+  is row-sharded): output row i needs a[., i, .] and ALL of b; each rank runs the
+  input phase on the token slab that yields its a and its share of b, b's chunks are
+  exchanged peer by peer and contracted as they arrive, and the output phase runs on
+  the rank's rows.
 
 * attention with pair bias: the bias is per query row, so rank r takes query rows
   [r*M/P, (r+1)*M/P) with its rows of z (the pair tensor, the only large input)
@@ -93,6 +95,12 @@ class TrimulKernelOps:
     """The sm_100a kernels for one rank's triangle-mul slab."""
 
     COL_TILE = 256  # contract_cols ranges start on (and span) multiples of this
+
+    @staticmethod
+    def contract(a, b, direction):
+        from .triangle_mul.kernel import contract
+
+        return contract(a, b, direction)
 
     @staticmethod
     def contract_cols(a, b_flat, direction, Mi, L, P, j0, jc, y):
@@ -207,9 +215,17 @@ def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
     return out.reshape(n, L, C)
 
 
-def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-5, group=None, ops=TrimulKernelOps):
+def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-5, group=None, ops=TrimulKernelOps,
+                                        split="auto"):
     """Rows [r0, r1) of the triangle multiplicative update of the replicated pair tensor
-    x (1, L, L, C); returns (1, n, L, C). Collective: all-gather of this rank's b."""
+    x (1, L, L, C); returns (1, n, L, C).
+
+    split="channels" (the default when C divides by the world size): every rank runs the
+    input phase on all tokens, contracts only its C/P channel planes (the contraction is
+    independent per channel) and one all-to-all brings each rank y of its rows, all
+    channels (C*L*L/P^2 elements to every peer). split="rows": the input phase on the
+    rank's share of tokens and b exchanged peer by peer under the row-slab contraction
+    (C*L*L*(P-1)/P elements per rank)."""
     if direction not in ("outgoing", "incoming"):
         raise ValueError(f"unknown direction: {direction!r} (expected 'outgoing'/'incoming')")
     B, L, _, C = x.shape
@@ -217,8 +233,31 @@ def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     r0, r1 = slab(L, rank, world)
+    if split not in ("auto", "channels", "rows"):
+        raise ValueError(f"unknown split: {split!r}")
+    if world > 1 and split != "rows" and C % world == 0 and hasattr(ops, "contract"):
+        return _trimul_channels(x, pre, direction, mask, eps, group, ops, rank, world)
     x_colsT = None if direction == "outgoing" else x[0, :, r0:r1].transpose(0, 1)
     return _trimul_from_slabs(x[0, r0:r1], x_colsT, pre, direction, mask, eps, group, ops).unsqueeze(0)
+
+
+def _trimul_channels(x, pre, direction, mask, eps, group, ops, rank, world):
+    """Channel-sharded triangle multiplication of the replicated x (1, L, L, C)."""
+    _, L, _, C = x.shape
+    n, cs = L // world, C // world
+    r0, r1 = rank * n, (rank + 1) * n
+    xs = x[0].reshape(L * L, C).contiguous()
+    ms = None if mask is None else mask.reshape(L * L)
+    ab = ops.input_phase(xs, ms, pre, eps)  # (2C, L*L) D-major: a = channels [0, C), b = [C, 2C)
+    d0 = rank * cs
+    a = ab[d0:d0 + cs].view(cs, 1, L, L)
+    b = ab[C + d0:C + d0 + cs].view(cs, 1, L, L)
+    y_mine = ops.contract(a, b, direction)  # this rank's channels of y, every row i
+    send = y_mine.reshape(cs, world, n, L).permute(1, 0, 2, 3).contiguous()  # [dest rank][d][i][j]
+    recv = torch.empty_like(send)  # [src rank][d of src][i of mine][j]: y of my rows, channel-major
+    dist.all_to_all_single(recv.view(-1), send.view(-1), group=group)
+    out = ops.output_phase(recv.view(C, n * L), x[0, r0:r1].reshape(n * L, C).contiguous(), pre, eps)
+    return out.reshape(1, n, L, C)
 
 
 def transpose_rows(x_rows, group=None):
