@@ -468,6 +468,13 @@ def profile_op(args):
         ws = K.project_rows(inp["X"], pre["W_qkvz"], pre["ln_w32"], pre["ln_b32"], pre["BZ"], H, D, N=n,
                             mask_rows=inp["mask"], scale=1 / math.sqrt(D))
         fn = lambda: K.attend_rows(ws, ws["bias"], H, D)  # noqa: E731
+    elif args.profile_op == "transition":
+        # the Pairformer pair transition over the (n, n, C) pair tensor, in place
+        x = rn(n, n, C)
+        w = dict(norm_weight=1 + 0.1 * rn(C), norm_bias=0.1 * rn(C), w1=rn(4 * C, C, sd=C**-0.5),
+                 w2=rn(4 * C, C, sd=C**-0.5), w3=rn(C, 4 * C, sd=(4 * C) ** -0.5))
+        pre = tops.transition.precompute(**w)
+        fn = lambda: tops.transition.forward(x, pre, out=x)  # noqa: E731
     elif args.profile_op == "triangle_mul":
         x = rn(1, n, n, C)
         v = torch.zeros(n, device=dev)
@@ -498,7 +505,7 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEF)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ops", action="store_true", help="skip the other two ops")
-    ap.add_argument("--profile-op", choices=["attn_kernel", "triangle_mul", "attn_pair_bias"], default=None,
+    ap.add_argument("--profile-op", choices=["attn_kernel", "transition", "triangle_mul", "attn_pair_bias"], default=None,
                     help="run only this op (the attention kernel at config 1, triangle_mul at config 3, "
                          "attn_pair_bias at config 2; size --n) for profiling, print its time")
     args = ap.parse_args()
