@@ -56,7 +56,10 @@ namespace tops {
 #define TOPS_POLY_PICK(c) ((c) % 3 == 1)  // pairs whose 2^x takes the polynomial (11 of 32)
 #endif
 
-template <int D, int TR>
+// KS (key split): the NT tiles of a CTA share one row, query block and head and take
+// NT consecutive ranges of the key blocks; their partial (O, l, max) are merged in the
+// epilogue. Used where there are few work units (attention with pair bias: one row).
+template <int D, int TR, bool KS = false>
 struct AttnCfg {
   static constexpr int NT = TR;                 // tiles (128 queries x 1 row) per CTA
   // warps: 0 and 1 TMA producers (ring A, ring B), 2..NT+1 S issuers, NT+2..2NT+1 PV
@@ -73,8 +76,9 @@ struct AttnCfg {
   static constexpr int PEN_BYTES = 16 * 128;    // MN-major 16 x 64 tile, row 0 = penalty row
   // ring A: the bias tile, the TR K tiles and the TR penalty tiles (free once every S
   // MMA of the block has run); ring B: the TR V^T tiles (free once every PV has run)
-  static constexpr int K_OFF = BIAS_BYTES;
-  static constexpr int PEN_OFF = BIAS_BYTES + TR * K_BYTES;
+  static constexpr int NBIAS = KS ? TR : 1;     // bias tiles per stage (KS: one per key range)
+  static constexpr int K_OFF = NBIAS * BIAS_BYTES;
+  static constexpr int PEN_OFF = K_OFF + TR * K_BYTES;
   static constexpr int A_BYTES = PEN_OFF + TR * PEN_BYTES;
   static constexpr int B_BYTES = TR * V_BYTES;
   static constexpr int NA = 3;
@@ -101,9 +105,9 @@ struct AttnArgs {
   int has_mask;  // penalty rows present (else every key < Nk is valid)
 };
 
-template <int D, int TR>
+template <int D, int TR, bool KS = false>
 struct AttnSmem {
-  using Cfg = AttnCfg<D, TR>;
+  using Cfg = AttnCfg<D, TR, KS>;
   alignas(1024) uint8_t q[Cfg::NT][Cfg::Q_BYTES];
   alignas(1024) uint8_t ring_a[Cfg::NA][Cfg::A_BYTES];
   alignas(1024) uint8_t ring_b[Cfg::NB][Cfg::B_BYTES];
@@ -121,6 +125,9 @@ struct AttnSmem {
   uint64_t pv_done[Cfg::NT][2];  // PV of a block using P buffer b finished (P reusable, O stable)
   uint64_t o_full[Cfg::NT];    // the last PV of the unit finished
   uint64_t o_empty[Cfg::NT];   // the epilogue has read O (the next unit may overwrite it)
+  // KS: tiles 1.. hand (O, l, max) of each query row to tile 0's epilogue
+  float comb[KS ? TR - 1 : 1][KS ? 128 * (D + 2) : 1];
+  uint64_t comb_full, comb_empty;
   uint32_t tmem_base;
   int abort;
 };
@@ -140,18 +147,23 @@ __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
 
 constexpr uint32_t kF16NegInf2 = 0xFC00FC00u;
 
-template <typename T, int D, int TR>
-__global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
+template <typename T, int D, int TR, bool KS = false>
+__global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_pen,
                 const __grid_constant__ CUtensorMap map_b, AttnArgs a) {
-  using Cfg = AttnCfg<D, TR>;
+  using Cfg = AttnCfg<D, TR, KS>;
   using E = Elem<T>;
   constexpr int NA = Cfg::NA, NB = Cfg::NB, NT = Cfg::NT, BK = Cfg::BK, NPB = Cfg::NPB;
   extern __shared__ uint8_t smem_raw[];
-  auto& sm = *reinterpret_cast<AttnSmem<D, TR>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto& sm = *reinterpret_cast<AttnSmem<D, TR, KS>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (a.Nk + BK - 1) / BK;
+  // key blocks per unit and tile: all of them, or (KS) this tile's share of them; tile t's
+  // key block at step j is kblk(t, j) (KS ranges past the last block are empty: TMA zero-fill,
+  // every key out of range)
+  const int nst = KS ? (nkb + NT - 1) / NT : nkb;
+  auto kblk = [&](int t, int j) { return KS ? t * nst + j : j; };
   const int H = a.H;
   const bool has_mask = a.has_mask != 0;
   auto k_tile = [&](int s, int r) { return sm.ring_a[s] + Cfg::K_OFF + r * Cfg::K_BYTES; };
@@ -198,6 +210,8 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       mbar_init(&sm.o_full[t], 1);
       mbar_init(&sm.o_empty[t], 4);
     }
+    mbar_init(&sm.comb_full, 128 * (NT - 1 > 0 ? NT - 1 : 1));
+    mbar_init(&sm.comb_empty, 128);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -215,14 +229,16 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
   // phases run on across units (g = blocks processed by this CTA so far, lu = units
   // so far), so the producers stream the next unit's tiles while the current one ends.
   const int n_qb = (a.Nq + 127) / 128;
-  const int n_rg = (a.R + TR - 1) / TR;
+  constexpr int UROWS = KS ? 1 : TR;  // pair rows per unit (KS: the tiles share one row)
+  const int n_rg = (a.R + UROWS - 1) / UROWS;
   const int n_units = n_qb * n_rg * a.H;
   auto coords = [&](int u, int& q0, int& row0, int& h) {
     q0 = (u % n_qb) * 128;
     const int rest = u / n_qb;
-    row0 = (rest % n_rg) * TR;
+    row0 = (rest % n_rg) * UROWS;
     h = rest / n_rg;
   };
+  auto trow = [&](int row0, int t) { return KS ? row0 : row0 + t; };  // pair row of tile t
 
   if (warp == 0) {
     // ---------------- TMA producer A: bias, K and penalty tiles (ring A), Q tiles ----------------
@@ -234,27 +250,29 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       tma_prefetch_desc(&map_b);
       if (has_mask) tma_prefetch_desc(&map_pen);
     }
-    const uint32_t a_tx = Cfg::BIAS_BYTES + NT * Cfg::K_BYTES + (has_mask ? NT * 128 : 0);
+    const uint32_t a_tx = Cfg::NBIAS * Cfg::BIAS_BYTES + NT * Cfg::K_BYTES + (has_mask ? NT * 128 : 0);
     bool ok = true;
     int g = 0, lu = 0;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nst) {
       int q0, row0, h;
       coords(u, q0, row0, h);
-      for (int j = 0; j < nkb; ++j) {
-        const int gg = g + j, s = gg % NA, k0 = j * BK;
+      for (int j = 0; j < nst; ++j) {
+        const int gg = g + j, s = gg % NA;
         if (!mbar_wait(&sm.a_empty[s], ((gg / NA) & 1) ^ 1, abort, 201)) { ok = false; break; }
         if (lane == 0) mbar_expect_tx(&sm.a_full[s], a_tx);
         __syncwarp();
-        if (lane == NT) tma_load_3d(sm.ring_a[s], &map_b, &sm.a_full[s], k0, q0, h);
-        else if (lane < NT) tma_load_3d(k_tile(s, lane), &map_k, &sm.a_full[s], 0, k0, (row0 + lane) * H + h);
+        if (lane >= NT && lane < NT + Cfg::NBIAS)
+          tma_load_3d(sm.ring_a[s] + (lane - NT) * Cfg::BIAS_BYTES, &map_b, &sm.a_full[s], kblk(lane - NT, j) * BK, q0, h);
+        else if (lane < NT)
+          tma_load_3d(k_tile(s, lane), &map_k, &sm.a_full[s], 0, kblk(lane, j) * BK, trow(row0, lane) * H + h);
         else if (has_mask && lane >= 16 && lane < 16 + NT)
-          tma_load_2d(pen_tile(s, lane - 16), &map_pen, &sm.a_full[s], k0, row0 + lane - 16);
+          tma_load_2d(pen_tile(s, lane - 16), &map_pen, &sm.a_full[s], kblk(lane - 16, j) * BK, trow(row0, lane - 16));
         if (j == 0) {
           // the unit's Q tiles, once the previous unit's last QK^T has read them
           if (!mbar_wait(&sm.q_empty, (lu & 1) ^ 1, abort, 213)) { ok = false; break; }
           if (lane == 0) mbar_expect_tx(&sm.bar_q, NT * Cfg::Q_BYTES);
           __syncwarp();
-          if (lane < NT) tma_load_3d(sm.q[lane], &map_q, &sm.bar_q, 0, q0, (row0 + lane) * H + h);
+          if (lane < NT) tma_load_3d(sm.q[lane], &map_q, &sm.bar_q, 0, q0, trow(row0, lane) * H + h);
         }
       }
     }
@@ -264,16 +282,16 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
     const uint32_t b_tx = NT * (D * 128);
     bool ok = true;
     int g = 0;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, g += nkb) {
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, g += nst) {
       int q0, row0, h;
       coords(u, q0, row0, h);
       (void)q0;
-      for (int j = 0; j < nkb; ++j) {
-        const int gg = g + j, sb = gg % NB, k0 = j * BK;
+      for (int j = 0; j < nst; ++j) {
+        const int gg = g + j, sb = gg % NB;
         if (!mbar_wait(&sm.b_empty[sb], ((gg / NB) & 1) ^ 1, abort, 211)) { ok = false; break; }
         if (lane == 0) mbar_expect_tx(&sm.b_full[sb], b_tx);
         __syncwarp();
-        if (lane < NT) tma_load_3d(v_tile(sb, lane), &map_v, &sm.b_full[sb], k0, 0, (row0 + lane) * H + h);
+        if (lane < NT) tma_load_3d(v_tile(sb, lane), &map_v, &sm.b_full[sb], kblk(lane, j) * BK, 0, trow(row0, lane) * H + h);
       }
     }
   } else if (warp <= NT + 1) {
@@ -288,14 +306,14 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       bool ok = true;
       int g = 0, lu = 0;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nst) {
         if (!mbar_wait(&sm.bar_q, lu & 1, abort, 202)) break;
-        for (int j = 0; j < nkb; ++j) {
+        for (int j = 0; j < nst; ++j) {
           const int gg = g + j, s = gg % NA;
           if (!mbar_wait(&sm.a_full[s], (gg / NA) & 1, abort, 203)) { ok = false; break; }
           if (gg > 0 && !mbar_wait(&sm.s_free[t], (gg - 1) & 1, abort, 204)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t ba = smem_u32(sm.ring_a[s]), ka = smem_u32(k_tile(s, t));
+          const uint32_t ba = smem_u32(sm.ring_a[s] + (KS ? t : 0) * Cfg::BIAS_BYTES), ka = smem_u32(k_tile(s, t));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             mma_ss(s_tmem, make_smem_desc(ba + kk * 32, 16, 1024, kSw128), make_smem_desc(ia + kk * 32, 16, 1024, kSw128),
@@ -308,7 +326,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
             mma_ss(s_tmem, ones_desc, make_smem_desc(smem_u32(pen_tile(s, t)), 2048, 1024, kSw128), idesc_pen, 1);
           mma_commit(&sm.s_full[t]);
           mma_commit(&sm.a_empty[s]);  // bias, K and penalty tiles consumed once these finish
-          if (j == nkb - 1) mma_commit(&sm.q_empty);  // Q of this unit no longer needed
+          if (j == nst - 1) mma_commit(&sm.q_empty);  // Q of this unit no longer needed
         }
       }
     }
@@ -322,8 +340,8 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       const uint32_t o_tmem = tbase + Cfg::O_COL + t * Cfg::NPV;
       bool ok = true;
       int g = 0, lu = 0;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
-        for (int j = 0; j < nkb; ++j) {
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nst) {
+        for (int j = 0; j < nst; ++j) {
           const int gg = g + j, sb = gg % NB;
           if (!mbar_wait(&sm.p_full[t], gg & 1, abort, 205)) { ok = false; break; }
           if (!mbar_wait(&sm.b_full[sb], (gg / NB) & 1, abort, 212)) { ok = false; break; }
@@ -336,7 +354,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk)
             mma_ts(o_tmem, p_tmem + kk * 8, make_smem_desc(vb + kk * 32, 16, 1024, kSw128), idesc_pv, j > 0 || kk > 0);
           mma_commit(&sm.pv_done[t][gg % NPB]);
-          if (j == nkb - 1) mma_commit(&sm.o_full[t]);
+          if (j == nst - 1) mma_commit(&sm.o_full[t]);
           mma_commit(&sm.b_empty[sb]);
         }
       }
@@ -350,11 +368,11 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
     const uint32_t oaddr = lane_addr + Cfg::O_COL + t * Cfg::NPV;
     bool ok = true;
     int g = 0, lu = 0;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nkb) {
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nst) {
       int q0, row0, h;
       coords(u, q0, row0, h);
       float m_use = 0.f;
-      for (int j = 0; j < nkb; ++j) {
+      for (int j = 0; j < nst; ++j) {
         const int gg = g + j;
         if (!mbar_wait(&sm.s_full[t], gg & 1, abort, 206)) { ok = false; break; }
         tc_fence_after();
@@ -364,7 +382,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.s_free[t]);
-        const int nvalid = a.Nk - j * BK;
+        const int nvalid = a.Nk - kblk(t, j) * BK;
         if (nvalid < BK) {
           // keys past Nk (zero-filled K, bias and penalty) are out of range: -inf
 #pragma unroll
@@ -442,7 +460,43 @@ __global__ void __launch_bounds__(AttnCfg<D, TR>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_empty[t]);
-      const int ri = row0 + t;
+      if constexpr (KS) {
+        // merge the key ranges: tiles 1.. hand (O, l, max) of their row to tile 0, which
+        // rescales each part to the common max (an all-masked part has max -inf: weight 0)
+        constexpr int W = D + 2;
+        if (t > 0) {
+          if (got && mbar_wait(&sm.comb_empty, (lu & 1) ^ 1, abort, 217)) {
+            float* c = sm.comb[t - 1] + qrow * W;
+#pragma unroll
+            for (int d = 0; d <= D; ++d) c[d] = __uint_as_float(o[d]);
+            c[D + 1] = m_use;
+          } else {
+            ok = false;
+          }
+          mbar_arrive(&sm.comb_full);
+          continue;
+        }
+        if (!(got && mbar_wait(&sm.comb_full, lu & 1, abort, 218))) {
+          ok = false;
+          continue;
+        }
+        float m = m_use;
+#pragma unroll
+        for (int t2 = 1; t2 < NT; ++t2) m = fmaxf(m, sm.comb[t2 - 1][qrow * W + D + 1]);
+        const float f0 = (m == -INFINITY || m_use == -INFINITY) ? 0.f : ex2_approx(m_use - m);
+#pragma unroll
+        for (int d = 0; d <= D; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * f0);
+#pragma unroll
+        for (int t2 = 1; t2 < NT; ++t2) {
+          const float* c = sm.comb[t2 - 1] + qrow * W;
+          const float mt = c[D + 1];
+          const float ft = (m == -INFINITY || mt == -INFINITY) ? 0.f : ex2_approx(mt - m);
+#pragma unroll
+          for (int d = 0; d <= D; ++d) o[d] = __float_as_uint(fmaf(c[d], ft, __uint_as_float(o[d])));
+        }
+        mbar_arrive(&sm.comb_empty);
+      }
+      const int ri = trow(row0, t);
       const int q = q0 + qrow;
       if (got && ri < a.R && q < a.Nq) {
         // l = 0: every key of the row is masked (attn_deadrow_kernel writes those rows)

@@ -52,7 +52,8 @@ extern "C" int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t M
   if (rc != TOPS_OK) return rc;
   // attention of query rows [q0, q0 + Mq): a row window of Q ([H][M][D], f16)
   const void* q_win = static_cast<const char*>(q_ws) + q0 * D * 2;
-  return run_attn<1>(dtype, static_cast<int>(D), 1, static_cast<int>(H), mq, m, mkp, q_win, k_ws, vt_ws, pen, bias_ws,
+  // one row: few work units, so each CTA's two tiles split the keys of one query block
+  return run_attn<2, true>(dtype, static_cast<int>(D), 1, static_cast<int>(H), mq, m, mkp, q_win, k_ws, vt_ws, pen, bias_ws,
                      og_rows, st, m);
 }
 

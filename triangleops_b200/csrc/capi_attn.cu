@@ -86,10 +86,10 @@ int run_proj(int dtype, int C, int D, bool ln, bool bp, const void* x, const voi
 // ---------------------------------------------------------------------------
 // attention
 // ---------------------------------------------------------------------------
-template <typename T, int D, int TR>
+template <typename T, int D, int TR, bool KS = false>
 int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt, const void* pen,
                 const void* bias, void* out, cudaStream_t st, int q_head_rows) {
-  using Cfg = AttnCfg<D, TR>;
+  using Cfg = AttnCfg<D, TR, KS>;
   const CUtensorMapSwizzle qk_sw = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   const CUtensorMapDataType f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv, mp, mb;
@@ -126,11 +126,12 @@ int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void
     if (!make_tmap(&mb, f16, 3, bias, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
   AttnArgs args{R, Nq, Nk, out, H, pen != nullptr ? 1 : 0};
-  const size_t smem = sizeof(AttnSmem<D, TR>) + 1024;
-  auto kern = attn_kernel<T, D, TR>;
+  const size_t smem = sizeof(AttnSmem<D, TR, KS>) + 1024;
+  auto kern = attn_kernel<T, D, TR, KS>;
   set_smem(kern, smem);
   // persistent: one CTA per SM (shared memory and TMEM allow no second), looping over units
-  const long long units = static_cast<long long>((Nq + 127) / 128) * ((R + TR - 1) / TR) * H;
+  constexpr int urows = KS ? 1 : TR;
+  const long long units = static_cast<long long>((Nq + 127) / 128) * ((R + urows - 1) / urows) * H;
   const int grid = units < sm_count() ? static_cast<int>(units) : sm_count();
   kern<<<grid, Cfg::THREADS, smem, st>>>(mq, mk, mv, mp, mb, args);
   if (cudaGetLastError() != cudaSuccess) return TOPS_ERR_CUDA;
@@ -148,7 +149,7 @@ int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void
 #ifndef TOPS_ATTN_TR
 #define TOPS_ATTN_TR 3
 #endif
-template <int TR>
+template <int TR, bool KS = false>
 int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void* q, const void* k, const void* vt,
              const void* pen, const void* bias, void* out, cudaStream_t st, int q_head_rows = 0) {
   // q_head_rows: rows per head of the Q buffer (Q may be a row window of a longer
@@ -156,11 +157,11 @@ int run_attn(int dtype, int D, int R, int H, int Nq, int Nk, int Nkp, const void
   if (q_head_rows == 0) q_head_rows = Nq;
   if (q_head_rows < Nq) return TOPS_ERR_SHAPE;
   if (dtype == TOPS_BF16) {
-    if (D == 32) return launch_attn<__nv_bfloat16, 32, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
-    if (D == 16) return launch_attn<__nv_bfloat16, 16, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 32) return launch_attn<__nv_bfloat16, 32, TR, KS>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 16) return launch_attn<__nv_bfloat16, 16, TR, KS>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
   } else if (dtype == TOPS_F16) {
-    if (D == 32) return launch_attn<__half, 32, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
-    if (D == 16) return launch_attn<__half, 16, TR>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 32) return launch_attn<__half, 32, TR, KS>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
+    if (D == 16) return launch_attn<__half, 16, TR, KS>(R, H, Nq, Nk, Nkp, q, k, vt, pen, bias, out, st, q_head_rows);
   }
   return TOPS_ERR_SHAPE;
 }
