@@ -13,14 +13,18 @@
 // rows ("tiles", 128 queries each) of the same head and query block: each bias tile
 // read from L2 serves TR rows.
 //
-// The tensor core builds S completely, so the softmax does per element only the max,
-// the subtraction and 2^x. Per 64-key block and tile, one thread issues into the f16
-// accumulator S:
+// The tensor core builds S completely, running max included, so the softmax does per
+// element only the block max and 2^x. Per 64-key block and tile, one thread issues into
+// the f16 accumulator S:
 //   S  = bias x I          4 MMAs (K = 64 keys in steps of 16; I = 64 x 64 identity)
 //   S += Q K^T             D/16 MMAs
-//   S += 1 x pen           1 MMA, masked calls only: A is a 128 x 16 tile of ones and
-//                          B an MN-major 16 x 64 tile whose row 0 is the pair row's
-//                          penalty row (rows 1..15 zero), so every query gets pen[k]
+//   S += M x pen           1 MMA: M is the tile's 128 x 16 "row term" tile (column 0
+//                          1.0, columns 1 and 2 the f16 pair hi + lo = -m of the query
+//                          row), B an MN-major 16 x 64 tile whose row 0 is the pair
+//                          row's penalty row and rows 1 and 2 ones, so every query gets
+//                          pen[k] - m. m is the running max the softmax last settled on
+//                          (0 at the start of a unit); the softmax rewrites its row of M
+//                          only when m moves, before it frees S for the next block.
 // and one thread issues PV: O += P V^T (P from TMEM, 4 MMAs of 16 keys).
 //
 // Cost model (measured on B200): a warp pays ~82 cycles to issue one SS tcgen05.mma
@@ -41,7 +45,8 @@
 //
 // Online softmax in the exp2 domain (Q carries scale*log2(e) and the bias log2(e),
 // both folded in upstream) with lazy rescaling (O is only rescaled when the running
-// max grows by more than 2^8). The per-element work runs on f16 pairs: the tensor
+// max grows by more than 2^8; the S the softmax loads is already x = s - m, so 2^x
+// needs no subtraction unless m moves in this block). The per-element work runs on f16 pairs: the tensor
 // core accumulates S in f16 (each step rounds once, relative error 2^-11, below the
 // 2^-8 rounding the 16-bit operands already put into S), the softmax loads it as
 // packed pairs (tcgen05.ld .pack::16b), takes the row max as a pairwise tree, and
@@ -112,7 +117,11 @@ struct AttnSmem {
   alignas(1024) uint8_t ring_a[Cfg::NA][Cfg::A_BYTES];
   alignas(1024) uint8_t ring_b[Cfg::NB][Cfg::B_BYTES];
   alignas(1024) uint8_t ident[64 * 128];   // f16 identity (64 x 64, K-major SW128)
-  alignas(1024) uint8_t ones[128 * 32];    // f16 ones (128 x 16, K-major)
+  // per tile: the A operand of the penalty / running-max MMA (128 x 16 f16, K-major
+  // SW32; row q = [1, -m_hi, -m_lo, 0, 0, 0, 0, 0] in both 16-byte halves, so the
+  // 32-byte swizzle, which may swap the halves, leaves the logical columns 0..2 and
+  // 8..10 equal; B rows 8..10 are zero)
+  alignas(1024) uint8_t mtile[Cfg::NT][128 * 32];
   uint64_t bar_q;
   uint64_t q_empty;            // one commit per S issuer (after the unit's last QK^T)
   uint64_t a_full[Cfg::NA];
@@ -172,24 +181,27 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
 
   // Constant operand parts, written once (TMA never touches them):
   //  * rows D .. NPV-1 of every V^T tile: row D all ones (the row-sum column of PV), the rest zero;
-  //  * rows 1..15 of every penalty tile (TMA fills row 0 only);
-  //  * the 64 x 64 identity (element (n, k) at n*128 + ((k/8 ^ n%8) * 16) + (k%8)*2) and the ones tile.
+  //  * every penalty tile: row 0 zero (TMA overwrites it on masked calls), rows 1 and 2
+  //    ones (they carry -m_hi and -m_lo of the row term tile), rows 3..15 zero;
+  //  * the 64 x 64 identity (element (n, k) at n*128 + ((k/8 ^ n%8) * 16) + (k%8)*2) and
+  //    the row term tiles (m = 0).
   constexpr int EXTRA_ROWS = Cfg::NPV - D;
   for (int idx = threadIdx.x; idx < NB * NT * EXTRA_ROWS * 32; idx += blockDim.x) {
     const int w = idx & 31, rowp = (idx >> 5) % EXTRA_ROWS, rs = idx / (EXTRA_ROWS * 32);
     uint32_t* v = reinterpret_cast<uint32_t*>(v_tile(rs / NT, rs % NT));
     v[(D + rowp) * 32 + w] = rowp == 0 ? 0x3C003C00u : 0u;
   }
-  for (int idx = threadIdx.x; idx < NA * NT * 15 * 32; idx += blockDim.x) {
-    const int w = idx & 31, rowp = (idx >> 5) % 15, rs = idx / (15 * 32);
-    reinterpret_cast<uint32_t*>(pen_tile(rs / NT, rs % NT))[(1 + rowp) * 32 + w] = 0u;
+  for (int idx = threadIdx.x; idx < NA * NT * 16 * 32; idx += blockDim.x) {
+    const int w = idx & 31, row = (idx >> 5) & 15, rs = idx / (16 * 32);
+    reinterpret_cast<uint32_t*>(pen_tile(rs / NT, rs % NT))[row * 32 + w] = (row == 1 || row == 2) ? 0x3C003C00u : 0u;
   }
   for (int w = threadIdx.x; w < 64 * 32; w += blockDim.x) {
     const int n = w >> 5, pc = w & 31;          // row n, 32-bit word pc of the 128-byte row
     const int k0 = ((pc >> 2) ^ (n & 7)) * 8 + (pc & 3) * 2;  // logical column of the word's low half
     reinterpret_cast<uint32_t*>(sm.ident)[w] = (k0 == n ? 0x3C00u : 0u) | (k0 + 1 == n ? 0x3C000000u : 0u);
   }
-  for (int w = threadIdx.x; w < 128 * 8; w += blockDim.x) reinterpret_cast<uint32_t*>(sm.ones)[w] = 0x3C003C00u;
+  for (int w = threadIdx.x; w < NT * 128 * 8; w += blockDim.x)
+    reinterpret_cast<uint32_t*>(&sm.mtile[0][0])[w] = (w & 3) == 0 ? 0x00003C00u : 0u;
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_q, 1);
     mbar_init(&sm.q_empty, NT);
@@ -302,7 +314,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
       const uint32_t idesc_s = make_idesc_f16(128, BK, 0, false, false) & ~(3u << 4);
       const uint32_t idesc_pen = make_idesc_f16(128, BK, 0, false, true) & ~(3u << 4);
       const uint32_t qa = smem_u32(sm.q[t]), ia = smem_u32(sm.ident);
-      const uint64_t ones_desc = make_smem_desc(smem_u32(sm.ones), 16, 256, kSw32);
+      const uint64_t mt_desc = make_smem_desc(smem_u32(sm.mtile[t]), 16, 256, kSw32);
       const uint32_t s_tmem = tbase + Cfg::S_COL + t * 64;
       bool ok = true;
       int g = 0, lu = 0;
@@ -322,8 +334,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
           for (int kk = 0; kk < D / 16; ++kk)
             mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
                    make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_s, 1);
-          if (has_mask)
-            mma_ss(s_tmem, ones_desc, make_smem_desc(smem_u32(pen_tile(s, t)), 2048, 1024, kSw128), idesc_pen, 1);
+          mma_ss(s_tmem, mt_desc, make_smem_desc(smem_u32(pen_tile(s, t)), 2048, 1024, kSw128), idesc_pen, 1);
           mma_commit(&sm.s_full[t]);
           mma_commit(&sm.a_empty[s]);  // bias, K and penalty tiles consumed once these finish
           if (j == nst - 1) mma_commit(&sm.q_empty);  // Q of this unit no longer needed
@@ -371,17 +382,16 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++lu, g += nst) {
       int q0, row0, h;
       coords(u, q0, row0, h);
-      float m_use = 0.f;
+      // m_use: the running max the P of this unit are relative to (-inf while every key seen
+      // is masked); m_b: the value baked into S by the row term tile (m_use once finite,
+      // 0 before: S then holds s itself)
+      float m_use = -INFINITY, m_b = 0.f;
       for (int j = 0; j < nst; ++j) {
         const int gg = g + j;
         if (!mbar_wait(&sm.s_full[t], gg & 1, abort, 206)) { ok = false; break; }
         tc_fence_after();
         uint32_t x[32];
-        tmem_ld64_pack16(lane_addr + Cfg::S_COL + t * 64, x);
-        // S consumed: the S MMAs of the next block may proceed
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.s_free[t]);
+        tmem_ld64_pack16(lane_addr + Cfg::S_COL + t * 64, x);  // x = s - m_b
         const int nvalid = a.Nk - kblk(t, j) * BK;
         if (nvalid < BK) {
           // keys past Nk (zero-filled K, bias and penalty) are out of range: -inf
@@ -398,21 +408,38 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
         for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
           for (int c = 0; c < w; ++c) mt[c] = hmax2_u(mt[c], mt[c + w]);
-        const float mx = fmaxf(f16lo(mt[0]), f16hi(mt[0]));
+        const float mxx = fmaxf(f16lo(mt[0]), f16hi(mt[0]));  // block max of s - m_b (f16 value)
+        // the max moves on the first finite key of the row and when it grows past m_use + 8
+        const bool need = m_use == -INFINITY ? mxx > -INFINITY : mxx > 8.0f;
+        const float m_new = need ? m_b + mxx : m_use;
+        // S of the next block (the next unit's first block after the last one) is built
+        // against m_next: rewrite this row of the row term tile when it differs from m_b,
+        // while no S MMA of this tile is in flight (before s_free)
+        const float m_next = j == nst - 1 || m_new == -INFINITY ? 0.f : m_new;
+        if (__any_sync(0xffffffffu, m_next != m_b)) {
+          const __half hi = __float2half_rn(-m_next);
+          const __half lo = __float2half_rn(-m_next - __half2float(hi));
+          const uint2 w = make_uint2(0x3C00u | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16),
+                                     static_cast<uint32_t>(__half_as_ushort(lo)));
+          uint2* mrow = reinterpret_cast<uint2*>(sm.mtile[t] + qrow * 32);
+          mrow[0] = w;
+          mrow[2] = w;
+          fence_proxy_async_smem();
+        }
+        // S consumed: the S MMAs of the next block may proceed
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[t]);
         // P(gg) reuses the buffer of PV(gg - NPB) and an O rescale needs O stable (PV(gg - 1)
         // done). The previous unit's PVs are all done (its epilogue waited for o_full).
         bool waited = false;
-        if (j == 0) {
-          m_use = mx;
-        } else {
-          const bool need = mx > m_use + 8.0f;
-          if (__any_sync(0xffffffffu, need)) {
+        if (__any_sync(0xffffffffu, need)) {
+          if (j > 0) {
             if (!mbar_wait(&sm.pv_done[t][(gg - 1) % NPB], ((gg - 1) / NPB) & 1, abort, 208)) { ok = false; break; }
             waited = true;
             tc_fence_after();
             // m_use = -inf (every key so far masked): O holds only zero-weighted terms
-            const float alpha = need ? ex2_approx(m_use - mx) : 1.0f;
-            if (need) m_use = mx;
+            const float alpha = need ? ex2_approx(m_use - m_new) : 1.0f;
             // 16 columns at a time (few live registers on this rare path)
 #pragma unroll
             for (int c0 = 0; c0 < Cfg::NPV; c0 += 16) {
@@ -423,18 +450,17 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
               tmem_st16(oaddr + c0, o);
             }
           }
+          // this block against the new max: x - (m_new - m_b) = x - mxx (an f16 value)
+          const __half2 d2 = __float2half2_rn(need ? mxx : 0.f);
+          const uint32_t dh = *reinterpret_cast<const uint32_t*>(&d2);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) x[c] = hsub2_u(x[c], dh);
         }
-        // m_use is an f16 value (or -inf while every key seen is masked: then every x is
-        // -inf too and P = 2^(x - 0) = 0)
-        const float m_sub = m_use == -INFINITY ? 0.0f : m_use;
-        const __half2 mh2 = __float2half2_rn(m_sub);
-        const uint32_t mh = *reinterpret_cast<const uint32_t*>(&mh2);
+        m_use = m_new;
+        m_b = m_next;
         uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const uint32_t d = hsub2_u(x[c], mh);
-          pk[c] = TOPS_POLY_PICK(c) ? ex2_poly_f16x2(d) : ex2_f16x2(d);
-        }
+        for (int c = 0; c < 32; ++c) pk[c] = TOPS_POLY_PICK(c) ? ex2_poly_f16x2(x[c]) : ex2_f16x2(x[c]);
         if (j >= NPB && !waited) {
           if (!mbar_wait(&sm.pv_done[t][gg % NPB], ((gg - NPB) / NPB) & 1, abort, 209)) { ok = false; break; }
           tc_fence_after();
