@@ -24,7 +24,8 @@
 //                          row's penalty row and rows 1 and 2 ones, so every query gets
 //                          pen[k] - m. m is the running max the softmax last settled on
 //                          (0 at the start of a unit); the softmax rewrites its row of M
-//                          only when m moves, before it frees S for the next block.
+//                          only when m moves; the S issuer issues the other MMAs of
+//                          the next block meanwhile and this one once m is settled.
 // and one thread issues PV: O += P V^T (P from TMEM, 4 MMAs of 16 keys).
 //
 // Cost model (measured on B200): a warp pays ~82 cycles to issue one SS tcgen05.mma
@@ -130,6 +131,7 @@ struct AttnSmem {
   uint64_t b_empty[Cfg::NB];   // one commit per PV issuer
   uint64_t s_full[Cfg::NT];    // S of the block complete
   uint64_t s_free[Cfg::NT];    // the softmax has loaded S (it may be overwritten)
+  uint64_t m_ready[Cfg::NT];   // the softmax has settled the block's max (row term tile written)
   uint64_t p_full[Cfg::NT];    // P of the block written
   uint64_t pv_done[Cfg::NT][2];  // PV of a block using P buffer b finished (P reusable, O stable)
   uint64_t o_full[Cfg::NT];    // the last PV of the unit finished
@@ -216,6 +218,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
     for (int t = 0; t < NT; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.s_free[t], 4);
+      mbar_init(&sm.m_ready[t], 4);
       mbar_init(&sm.p_full[t], 4);
       mbar_init(&sm.pv_done[t][0], 1);
       mbar_init(&sm.pv_done[t][1], 1);
@@ -334,6 +337,9 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
           for (int kk = 0; kk < D / 16; ++kk)
             mma_ss(s_tmem, make_smem_desc(qa + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW),
                    make_smem_desc(ka + kk * 32, 16, Cfg::QK_SBO, Cfg::QK_SW), idesc_s, 1);
+          // the row term of S(gg) carries the max the softmax settled on in block gg - 1: the
+          // six MMAs above do not need it and run while the softmax takes that block's max
+          if (gg > 0 && !mbar_wait(&sm.m_ready[t], (gg - 1) & 1, abort, 215)) { ok = false; break; }
           mma_ss(s_tmem, mt_desc, make_smem_desc(smem_u32(pen_tile(s, t)), 2048, 1024, kSw128), idesc_pen, 1);
           mma_commit(&sm.s_full[t]);
           mma_commit(&sm.a_empty[s]);  // bias, K and penalty tiles consumed once these finish
@@ -392,6 +398,10 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
         tc_fence_after();
         uint32_t x[32];
         tmem_ld64_pack16(lane_addr + Cfg::S_COL + t * 64, x);  // x = s - m_b
+        // S consumed: the S MMAs of the next block may proceed (all but its row term)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[t]);
         const int nvalid = a.Nk - kblk(t, j) * BK;
         if (nvalid < BK) {
           // keys past Nk (zero-filled K, bias and penalty) are out of range: -inf
@@ -413,8 +423,8 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
         const bool need = m_use == -INFINITY ? mxx > -INFINITY : mxx > 8.0f;
         const float m_new = need ? m_b + mxx : m_use;
         // S of the next block (the next unit's first block after the last one) is built
-        // against m_next: rewrite this row of the row term tile when it differs from m_b,
-        // while no S MMA of this tile is in flight (before s_free)
+        // against m_next: rewrite this row of the row term tile when it differs from m_b
+        // (the row term MMA of this block has finished, the next one waits for m_ready)
         const float m_next = j == nst - 1 || m_new == -INFINITY ? 0.f : m_new;
         if (__any_sync(0xffffffffu, m_next != m_b)) {
           const __half hi = __float2half_rn(-m_next);
@@ -426,10 +436,8 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
           mrow[2] = w;
           fence_proxy_async_smem();
         }
-        // S consumed: the S MMAs of the next block may proceed
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.s_free[t]);
+        if (lane == 0) mbar_arrive(&sm.m_ready[t]);
         // P(gg) reuses the buffer of PV(gg - NPB) and an O rescale needs O stable (PV(gg - 1)
         // done). The previous unit's PVs are all done (its epilogue waited for o_full).
         bool waited = false;
