@@ -63,6 +63,8 @@ def _worker(rank, world, port, q):
         full = tdist.all_gather_rows(out.contiguous(), 0)
         if rank == 0:
             q.put(full)
+        # every rank done before any tears down (gloo teardown races otherwise)
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
@@ -135,6 +137,8 @@ def _trimul_worker(rank, world, port, q, direction, split):
         full = tdist.all_gather_rows(out[0].contiguous(), 0)
         if rank == 0:
             q.put(full)
+        # every rank done before any tears down (gloo teardown races otherwise)
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
@@ -236,6 +240,8 @@ def _apb_worker(rank, world, port, q):
         full = tdist.all_gather_rows(out.contiguous(), 0)
         if rank == 0:
             q.put(full)
+        # every rank done before any tears down (gloo teardown races otherwise)
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
@@ -300,6 +306,8 @@ def _chain_worker(rank, world, port, q):
         full = tdist.all_gather_rows(out.contiguous(), 0)
         if rank == 0:
             q.put(full)
+        # every rank done before any tears down (gloo teardown races otherwise)
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
