@@ -7,10 +7,8 @@
 // [attn_pair_bias/module.py:29-35, attn_pair_bias/kernel.py:149-185]. The reference
 // recomputes this inside the attention loop once per head (z read H times); here
 // z streams through shared memory by TMA, the tensor core takes the head dots and one
-// thread per token the statistics (16-byte vector loads, 256 contiguous bytes per
-// token), merge their partial statistics with warp-shuffle Welford (Chan's
-// pairwise update for equal counts) and reduce the H dot products in the same
-// shuffle tree. The logits are stored as f16 in log2 units, the operand format of the
+// thread per token the statistics (16-byte vector loads from the staged tile, two passes
+// over its row in registers with eight independent accumulation chains). The logits are stored as f16 in log2 units, the operand format of the
 // attention kernel (the reference adds them in fp32; f16 keeps 11 bits, |error| below
 // 2^-11 of the logit).
 #include "sm100.cuh"
@@ -144,15 +142,32 @@ __global__ void __launch_bounds__(kZbThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[s]);
+      // eight independent add chains (four packed fp32 pairs) per moment, not one 128-long
+      // dependent chain: the statistics keep pace with the TMA stream
+      unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+      for (int e = 0; e < 64; ++e) acc[e & 3] = f2_add(acc[e & 3], f2_pack(E::lo(p[e]), E::hi(p[e])));
       float sum = 0.f;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) sum += E::lo(p[e]) + E::hi(p[e]);
+      for (int e = 0; e < 4; ++e) {
+        float lo, hi;
+        f2_unpack(acc[e], lo, hi);
+        sum += lo + hi;
+        acc[e] = 0ull;
+      }
       const float mean = sum * (1.0f / CZ);
-      float m2 = 0.f;
+      const unsigned long long nm = f2_pack(-mean, -mean);
 #pragma unroll
       for (int e = 0; e < 64; ++e) {
-        const float d0 = E::lo(p[e]) - mean, d1 = E::hi(p[e]) - mean;
-        m2 = fmaf(d0, d0, fmaf(d1, d1, m2));
+        const unsigned long long dd = f2_add(f2_pack(E::lo(p[e]), E::hi(p[e])), nm);
+        acc[e & 3] = f2_fma(dd, dd, acc[e & 3]);
+      }
+      float m2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float lo, hi;
+        f2_unpack(acc[e], lo, hi);
+        m2 += lo + hi;
       }
       const float rstd = rsqrtf(m2 * (1.0f / CZ) + a.eps);
       if (!mbar_wait(&sm.acc_full[b], (it >> 1) & 1, abort, 605)) break;
