@@ -28,7 +28,7 @@ struct ZBiasArgs {
 
 constexpr int kZbTile = 128;        // tokens per tile (one TMEM lane each)
 constexpr int kZbStages = 5;        // tiles in flight per SM (32 KB each)
-constexpr int kZbThreads = 256;     // w0 TMA, w1 MMA, w4..w7 statistics / epilogue
+constexpr int kZbThreads = 384;     // w0 TMA, w1 MMA, w4..w7 and w8..w11 statistics / epilogue (even / odd tiles)
 
 struct ZbSmem {
   alignas(1024) uint8_t tile[kZbStages][2][16384];  // z tile: 128 tokens x 128 ch, two SW128 atoms
@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(kZbThreads, 1)
       }
     }
   } else if (warp >= 4) {
+    // two warpgroups take the tiles in turn (tile it uses accumulator it & 1)
+    const int wg = (warp - 4) >> 2;
     const int wq = warp & 3, r = wq * 32 + lane;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(wq * 32) << 16);
     float sw[H], bc[H];
@@ -130,6 +132,7 @@ __global__ void __launch_bounds__(kZbThreads, 1)
     int it = 0;
     for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int s = it % kZbStages, b = it & 1;
+      if (b != wg) continue;
       if (!mbar_wait(&sm.full[s], (it / kZbStages) & 1, abort, 604)) break;
       uint32_t p[64];
 #pragma unroll
