@@ -80,13 +80,22 @@ int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, cons
     if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
     if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
+  // y [nb][Mi][L], written in 32 x 32 boxes (64-byte swizzle) by the epilogue warps
+  CUtensorMap my;
+  {
+    const uint64_t dy[3] = {static_cast<uint64_t>(L), static_cast<uint64_t>(Mi), static_cast<uint64_t>(nb)};
+    const uint64_t sy[2] = {L * e, static_cast<uint64_t>(Mi) * L * e};
+    const uint32_t by[3] = {32, 32, 1};
+    if (!make_tmap(&my, tmap_dtype(dtype), 3, y, dy, sy, by, CU_TENSOR_MAP_SWIZZLE_64B)) return TOPS_ERR_TMAP;
+  }
   CtArgs args{L, nb, y, Mi, nc, j_begin, j_end};
+  static_assert(sizeof(CtSmem) + 1024 <= 227 * 1024, "contraction shared memory");
   const size_t smem = sizeof(CtSmem) + 1024;
   auto kern = trimul_contract_kernel<T, MN>;
   set_smem(kern, smem);
   const long long tiles = static_cast<long long>((Mi + kCtBM - 1) / kCtBM) * ((j_end - j_begin + kCtBN - 1) / kCtBN) * nb;
   const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
-  kern<<<grid, 384, smem, st>>>(ma, mb, args);
+  kern<<<grid, 384, smem, st>>>(ma, mb, my, args);
   return launch_status();
 }
 

@@ -427,13 +427,18 @@ __global__ void __launch_bounds__(128 + 128 + 128 * kInEpiWG, 1)
 // A 256 x 256 tile is two M=128 MMAs sharing each B tile: 2 x 256 TMEM columns
 // (all of TMEM, one accumulator pair). The larger tile halves the operand bytes per
 // FLOP against 128 x 256, which is what the stage ring can keep in flight from L2;
-// the epilogue (8 warps, one per TMEM lane quarter and row half) is short next to
-// the K loop, so the accumulator is not double-buffered.
+// the accumulator is not double-buffered. The epilogue (8 warps, one per TMEM lane
+// quarter and row half) stages each 32 x 32 chunk of y in shared memory (64-byte
+// swizzle) and writes it with one TMA store, so a warp's stores are 2 KB boxes rather
+// than 32 scattered row segments, and it releases the accumulator after its last TMEM
+// load, before the stores drain.
 constexpr int kCtBM = 256, kCtBN = 256, kCtBK = 64, kCtStages = 3;
+constexpr int kCtStageBytes = 32 * 32 * 2;  // one warp's 32 rows x 32 columns of y
 
 struct CtSmem {
   alignas(1024) uint8_t a[kCtStages][kCtBM * kCtBK * 2];
   alignas(1024) uint8_t b[kCtStages][kCtBN * kCtBK * 2];
+  alignas(1024) uint8_t ystage[8][2][kCtStageBytes];  // [epilogue warp][double buffer]
   uint64_t full[kCtStages], empty[kCtStages], acc_full, acc_empty;
   uint32_t tmem_base;
   int abort;
@@ -450,7 +455,7 @@ struct CtArgs {
 template <typename T, bool MN>
 __global__ void __launch_bounds__(384, 1)
     trimul_contract_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                           CtArgs a) {
+                           const __grid_constant__ CUtensorMap map_y, CtArgs a) {
   using E = Elem<T>;
   extern __shared__ uint8_t smem_raw[];
   CtSmem& sm = *reinterpret_cast<CtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -549,36 +554,52 @@ __global__ void __launch_bounds__(384, 1)
     const int m = (warp - 4) >> 2, wq = warp & 3;
     const int row = m * 128 + wq * 32 + lane;
     const uint32_t lane_addr = tbase + m * 256 + (static_cast<uint32_t>(wq * 32) << 16);
-    int it = 0;
+    uint8_t* stage0 = sm.ystage[warp - 4][0];
+    // 64-byte swizzle: the 16-byte chunk q of row r sits at chunk q ^ ((r >> 1) & 3)
+    const int sw = (lane >> 1) & 3;
+    int it = 0, nst = 0;
     for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       if (!mbar_wait(&sm.acc_full, it & 1, abort, 504)) break;
       tc_fence_after();
       int bb, i0, j0;
       decode(tile, bb, i0, j0);
-      const int i = i0 + row;
+      const int i = i0 + row, r0 = i0 + m * 128 + wq * 32;
       T* dst = static_cast<T*>(a.y) + (static_cast<size_t>(bb) * a.Mi + i) * a.L + j0;
 #pragma unroll 1
       for (int c0 = 0; c0 < kCtBN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + c0, r);
-        if (i < a.Mi) {
-          uint32_t p[16];
+        if (c0 + 32 == kCtBN) {  // the accumulator is free once its last columns are in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty);
+        }
+        if (r0 >= a.Mi) continue;
+        uint32_t p[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) p[e] = E::pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-          if (j0 + c0 + 32 <= a.j_end) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+        for (int e = 0; e < 16; ++e) p[e] = E::pack2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+        if (j0 + c0 + 32 <= a.j_end) {
+          uint8_t* buf = stage0 + (nst & 1) * kCtStageBytes;
+          if (lane == 0) bulk_wait_read1();  // the store that last read this buffer is done reading
+          __syncwarp();
 #pragma unroll
-            for (int q = 0; q < 4; ++q) d4[q] = make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
-          } else {
-            for (int e = 0; e < 32; ++e)
-              if (j0 + c0 + e < a.j_end) dst[c0 + e] = E::from_f(__uint_as_float(r[e]));
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ sw) << 4)) =
+                make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&map_y, buf, j0 + c0, r0, bb);  // rows >= Mi are clipped by the map
+            bulk_commit();
           }
+          ++nst;
+        } else if (i < a.Mi) {
+          for (int e = 0; e < 32; ++e)
+            if (j0 + c0 + e < a.j_end) dst[c0 + e] = E::from_f(__uint_as_float(r[e]));
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty);
     }
+    if (lane == 0) bulk_wait0();
   }
   tc_fence_before();
   __syncthreads();
