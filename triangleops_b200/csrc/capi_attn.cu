@@ -126,6 +126,7 @@ int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void
     if (!make_tmap(&mb, f16, 3, bias, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   }
   AttnArgs args{R, Nq, Nk, out, H, pen != nullptr ? 1 : 0};
+  static_assert(sizeof(AttnSmem<D, TR, KS>) + 1024 <= 227 * 1024, "attention shared memory");
   const size_t smem = sizeof(AttnSmem<D, TR, KS>) + 1024;
   auto kern = attn_kernel<T, D, TR, KS>;
   set_smem(kern, smem);
