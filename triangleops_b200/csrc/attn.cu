@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(AttnCfg<D, TR, KS>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   auto& sm = *reinterpret_cast<AttnSmem<D, TR, KS>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();  // the kernel after this one (the gate) may set itself up on SMs left free
   const int nkb = (a.Nk + BK - 1) / BK;
   // key blocks per unit and tile: all of them, or (KS) this tile's share of them; tile t's
   // key block at step j is kblk(t, j) (KS ranges past the last block are empty: TMA zero-fill,
@@ -562,6 +563,7 @@ __global__ void __launch_bounds__(128) attn_deadrow_kernel(const __half* __restr
                                                            const __half* __restrict__ vt, T* __restrict__ out, int R,
                                                            int Nq, int Nk, int Nkp, int HD) {
   using E = Elem<T>;
+  pdl_trigger();
   for (int r = blockIdx.x; r < R; r += gridDim.x) {
     const __half* prow = pen + static_cast<size_t>(r) * Nkp;
     bool alive = false;

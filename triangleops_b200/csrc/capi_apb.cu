@@ -7,11 +7,14 @@
 namespace tops {
 
 template <typename T>
-int launch_zbias(int dtype, const void* z, const ZBiasArgs& args, cudaStream_t st) {
+int launch_zbias(int dtype, const void* z, const ZBiasArgs& args, cudaStream_t st, int reserve_sms) {
   CUtensorMap mz;
   if (!map_rows(&mz, dtype, z, args.n_tok, 128, kZbTile)) return TOPS_ERR_TMAP;
   const long long tiles = (args.n_tok + kZbTile - 1) / kZbTile;
-  const int grid = tiles < sm_count() ? static_cast<int>(tiles) : sm_count();
+  // persistent, leaving reserve_sms SMs to the token projection that runs beside it
+  int sms = sm_count() - reserve_sms;
+  if (sms < sm_count() / 2) sms = sm_count() / 2;
+  const int grid = tiles < sms ? static_cast<int>(tiles) : sms;
   const size_t smem = sizeof(ZbSmem) + 1024;
   auto kern = zbias_kernel<T, 128, 4>;
   set_smem(kern, smem);
@@ -39,15 +42,19 @@ extern "C" int tops_apb_forward_rows(int dtype, int64_t M, int64_t q0, int64_t M
   const int m = static_cast<int>(M), mq = static_cast<int>(Mq);
   const int mkp = (m + 7) & ~7;
   ZBiasArgs za{static_cast<long long>(Mq) * M, m, mkp, mq, eps, wc, sum_w, b_const, static_cast<__half*>(bias_ws)};
-  int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(dtype, z_rows, za, st)
-                              : launch_zbias<__half>(dtype, z_rows, za, st);
+  // the projection's CTAs (one per 128 tokens) run on SMs the z-bias kernel leaves free
+  const int proj_ctas = (m + 127) / 128;
+  int rc = dtype == TOPS_BF16 ? launch_zbias<__nv_bfloat16>(dtype, z_rows, za, st, proj_ctas)
+                              : launch_zbias<__half>(dtype, z_rows, za, st, proj_ctas);
   if (rc != TOPS_OK) return rc;
   // Q/K/V projection of the whole (replicated, M x C) sequence: K/V are needed for
   // every key, and Q for all M rows costs less than a gather of the window; the
   // key mask becomes the penalty row (0 / -inf) the attention adds to every score.
+  // Launched programmatically beside the z-bias kernel (it reads none of its output).
   void* pen = key_mask != nullptr ? pen_ws : nullptr;
   ProjArgs pa{m, m, 1, mkp, scale * kLog2e, eps, nullptr, nullptr, nullptr, key_mask, nullptr, q_ws, k_ws, vt_ws, pen,
               nullptr};
+  pa.pdl = 1;
   rc = run_proj(dtype, static_cast<int>(C), static_cast<int>(D), false, false, x, w_qkv, pa, st);
   if (rc != TOPS_OK) return rc;
   // attention of query rows [q0, q0 + Mq): a row window of Q ([H][M][D], f16)

@@ -1,6 +1,7 @@
 // capi_attn.cu — C-ABI entry points of the attention ops (triangle attention,
 // fused gate, attention with pair bias). Declared in include/triangleops_b200.h.
 #include <cuda_runtime.h>
+#include <utility>
 #include "sm100.cuh"
 #include "status.h"
 #include "tmap.h"
@@ -27,6 +28,25 @@ inline int launch_status() { return cudaGetLastError() == cudaSuccess ? TOPS_OK 
 template <typename K>
 inline void set_smem(K kernel, size_t bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+// Launch with programmatic stream serialization: the kernel may be scheduled while the
+// previous kernel in the stream still runs (from that kernel's pdl_trigger, or its exit
+// when it has none); the kernel orders its reads of that kernel's results with pdl_wait.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // 2-D row-major [rows][C] operand, 128-row x 64-column boxes, 128B swizzle
@@ -59,7 +79,10 @@ int launch_proj(int dtype, const void* x, const void* w, const ProjArgs& args, c
   set_smem(kern, smem);
   const int tiles = args.trans ? args.R * ((args.Nk + 127) / 128) : (args.T + 127) / 128;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, 512, smem, st>>>(mx, mw, args);
+  if (args.pdl)
+    launch_pdl(kern, grid, 512, smem, st, mx, mw, args);
+  else
+    kern<<<grid, 512, smem, st>>>(mx, mw, args);
   return launch_status();
 }
 
@@ -184,7 +207,9 @@ int launch_gate(int dtype, int64_t T_, const void* o, const void* gin, const voi
   set_smem(kern, smem);
   const int tiles = static_cast<int>((T_ + 127) / 128);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, 640, smem, st>>>(mg, mo, mwg, mwo, args);
+  // scheduled early (its prologue and weight loads overlap the end of the attention);
+  // the kernel waits for the previous kernel's results before it reads O or the residual
+  launch_pdl(kern, grid, 640, smem, st, mg, mo, mwg, mwo, args);
   return launch_status();
 }
 

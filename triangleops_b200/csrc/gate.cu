@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(640, 1)
         tma_load_2d(sm.wg + ka * C * 128, &map_wg, &sm.bar_w, ka * 64, 0);
         tma_load_2d(sm.wo + ka * C * 128, &map_wo, &sm.bar_w, ka * 64, 0);
       }
+      pdl_wait();  // O and x~ come from the kernels before this one
       int it = 0;
       for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(640, 1)
       }
     }
   } else if (warp >= 4) {
+    pdl_wait();  // the residual may be the previous kernel's output
     const int wg = (warp - 4) >> 3;           // tile slot (alternate tiles)
     const int wq = warp & 3;
     const int half = ((warp - 4) >> 2) & 1;  // column half of the slot's tile

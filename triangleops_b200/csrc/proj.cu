@@ -54,6 +54,8 @@ struct ProjArgs {
   void* pen;           // [R][Nkp] f16 (nullptr = not written)
   void* bp;
   int trans;           // 1: token (i, k) is x[k][i] of a square [Nk][Nk] pair array (ending node)
+  int pdl;             // 1: launched to run beside the previous kernel (it reads none of that
+                       // kernel's results); the CTAs exit only once that kernel has completed
 };
 
 // Token tiles. Row-major input: 128 consecutive tokens of the flattened stream.
@@ -316,6 +318,9 @@ __global__ void __launch_bounds__(512, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tbase, Cfg::TMEM_COLS);
+  // a kernel that follows this one in the stream then also follows the kernel this one
+  // ran beside (no-op without programmatic launch)
+  pdl_wait();
 }
 
 }  // namespace tops

@@ -123,6 +123,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ----------------------------------------------------------------------------
+// programmatic dependent launch
+// ----------------------------------------------------------------------------
+// pdl_trigger: the kernel launched after this one in the stream with programmatic
+// stream serialization may be scheduled now (on SMs this grid leaves free).
+// pdl_wait: wait until the grid this one depends on has completed and its memory is
+// visible; returns at once when the kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ----------------------------------------------------------------------------
 // fences
 // ----------------------------------------------------------------------------
 // generic-proxy smem writes -> visible to the async proxy (TMA / tensor core)

@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(kZbThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   ZbSmem& sm = *reinterpret_cast<ZbSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();  // the token projection (launched next, programmatically) runs beside this kernel
   const long long n_tiles = (a.n_tok + kZbTile - 1) / kZbTile;
   // B tile: element (n, c) of the K-major SW128 layout at atom c/64, n*128 + ((c%64/8 ^ n%8)*16) + (c%8)*2
   for (int idx = threadIdx.x; idx < 16 * CZ; idx += blockDim.x) {
