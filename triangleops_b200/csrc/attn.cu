@@ -568,6 +568,9 @@ __global__ void __launch_bounds__(128) attn_deadrow_kernel(const __half* __restr
     const __half* prow = pen + static_cast<size_t>(r) * Nkp;
     bool alive = false;
     for (int k = threadIdx.x; k < Nk; k += blockDim.x) alive |= __half_as_ushort(prow[k]) == 0;
+    // the vote reads only the projection's penalty row; a dead row's output overwrites
+    // what the attention kernel (launched just before, still running) writes there
+    pdl_wait();
     if (__syncthreads_or(alive)) continue;
     // dead row: thread c (< H*D) owns value column c = h*D + d, V^T row (r*H + h)*D + d
     float mean = 0.f;

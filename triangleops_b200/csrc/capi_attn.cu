@@ -162,8 +162,9 @@ int launch_attn(int R, int H, int Nq, int Nk, int Nkp, const void* q, const void
   if (pen != nullptr) {
     // rows whose keys are all masked (rare: one vote per row, work only for dead rows)
     const int grid_d = R < 4 * sm_count() ? R : 4 * sm_count();
-    attn_deadrow_kernel<T><<<grid_d, 128, 0, st>>>(static_cast<const __half*>(pen), static_cast<const __half*>(vt),
-                                                   static_cast<T*>(out), R, Nq, Nk, Nkp, H * D);
+    // launched programmatically: the vote runs beside the attention where SMs are free
+    launch_pdl(attn_deadrow_kernel<T>, grid_d, 128, 0, st, static_cast<const __half*>(pen),
+               static_cast<const __half*>(vt), static_cast<T*>(out), R, Nq, Nk, Nkp, H * D);
   }
   return launch_status();
 }
