@@ -54,8 +54,14 @@ template <typename T, bool MN>
 int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, const void* b, void* y, cudaStream_t st,
                     int j_begin, int j_end) {
   CUtensorMap ma, mb;
+  int a_groups = 0;
   const int nc = L / P;
   const uint64_t e = 2;
+  // a 256-column tile of B stays inside one rank-major chunk: one box per stage
+  int b_one = (P == 1 || nc % kCtBN == 0) && nc % 64 == 0 ? 1 : 0;
+  // MN-major B: one grouped 5-D box measured slower than four 64-column boxes (1.63 vs
+  // 1.56 ms at L = 2048), so that path keeps the four loads
+  constexpr int b_one_mn = 0;
   if (!MN) {
     // A [nb][Mi][L] (K = L contiguous); B: P chunks of [nb][nc][L]
     const uint64_t da[3] = {static_cast<uint64_t>(L), static_cast<uint64_t>(Mi), static_cast<uint64_t>(nb)};
@@ -64,21 +70,39 @@ int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, cons
     const uint64_t db[4] = {static_cast<uint64_t>(L), static_cast<uint64_t>(nc), static_cast<uint64_t>(nb),
                             static_cast<uint64_t>(P)};
     const uint64_t sb[3] = {L * e, static_cast<uint64_t>(nc) * L * e, static_cast<uint64_t>(nb) * nc * L * e};
-    const uint32_t bbx[4] = {kCtBK, 128, 1, 1};
+    const uint32_t bbx[4] = {kCtBK, b_one ? static_cast<uint32_t>(kCtBN) : 128u, 1, 1};
     if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
     if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
   } else {
-    // A [nb][L][Mi] (M = i contiguous); B: P chunks of [nb][L][nc]
-    const uint64_t da[3] = {static_cast<uint64_t>(Mi), static_cast<uint64_t>(L), static_cast<uint64_t>(nb)};
-    const uint64_t sa[2] = {static_cast<uint64_t>(Mi) * e, static_cast<uint64_t>(Mi) * L * e};
-    const uint32_t bx[3] = {64, kCtBK, 1};
+    // A [nb][L][Mi] (M = i contiguous) viewed as {i mod 64, k, i / 64, nb}: one box of
+    // {64, BK, BM / 64, 1} is the whole MN-major tile, its four 64-row groups 8 KB apart
+    // (Mi % 64 == 0 on this path; else four 3-D boxes, one per group)
+    const bool a4 = Mi % 64 == 0;
+    const uint64_t da[4] = {64, static_cast<uint64_t>(L), static_cast<uint64_t>(Mi) / 64, static_cast<uint64_t>(nb)};
+    const uint64_t sa[3] = {static_cast<uint64_t>(Mi) * e, 128, static_cast<uint64_t>(Mi) * L * e};
+    const uint32_t bx[4] = {64, kCtBK, kCtBM / 64, 1};
+    const uint64_t da3[3] = {static_cast<uint64_t>(Mi), static_cast<uint64_t>(L), static_cast<uint64_t>(nb)};
+    const uint64_t sa3[2] = {static_cast<uint64_t>(Mi) * e, static_cast<uint64_t>(Mi) * L * e};
+    const uint32_t bx3[3] = {64, kCtBK, 1};
     const uint64_t db[4] = {static_cast<uint64_t>(nc), static_cast<uint64_t>(L), static_cast<uint64_t>(nb),
                             static_cast<uint64_t>(P)};
     const uint64_t sb[3] = {static_cast<uint64_t>(nc) * e, static_cast<uint64_t>(nc) * L * e,
                             static_cast<uint64_t>(nb) * nc * L * e};
     const uint32_t bbx[4] = {64, kCtBK, 1, 1};
-    if (!make_tmap(&ma, tmap_dtype(dtype), 3, a, da, sa, bx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
-    if (!make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B)) return TOPS_ERR_TMAP;
+    // grouped view of B as for A: {j mod 64, k, j / 64 within the chunk, nb, chunk}
+    const uint64_t db5[5] = {64, static_cast<uint64_t>(L), static_cast<uint64_t>(nc) / 64, static_cast<uint64_t>(nb),
+                             static_cast<uint64_t>(P)};
+    const uint64_t sb5[4] = {static_cast<uint64_t>(nc) * e, 128, static_cast<uint64_t>(nc) * L * e,
+                             static_cast<uint64_t>(nb) * nc * L * e};
+    const uint32_t bbx5[5] = {64, kCtBK, kCtBN / 64, 1, 1};
+    if (a4 ? !make_tmap(&ma, tmap_dtype(dtype), 4, a, da, sa, bx, CU_TENSOR_MAP_SWIZZLE_128B)
+           : !make_tmap(&ma, tmap_dtype(dtype), 3, a, da3, sa3, bx3, CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOPS_ERR_TMAP;
+    if (b_one_mn ? !make_tmap(&mb, tmap_dtype(dtype), 5, b, db5, sb5, bbx5, CU_TENSOR_MAP_SWIZZLE_128B)
+                 : !make_tmap(&mb, tmap_dtype(dtype), 4, b, db, sb, bbx, CU_TENSOR_MAP_SWIZZLE_128B))
+      return TOPS_ERR_TMAP;
+    a_groups = a4 ? 1 : 0;
+    b_one = b_one_mn;
   }
   // y [nb][Mi][L], written in 32 x 32 boxes (64-byte swizzle) by the epilogue warps
   CUtensorMap my;
@@ -88,7 +112,7 @@ int launch_contract(int dtype, int nb, int Mi, int L, int P, const void* a, cons
     const uint32_t by[3] = {32, 32, 1};
     if (!make_tmap(&my, tmap_dtype(dtype), 3, y, dy, sy, by, CU_TENSOR_MAP_SWIZZLE_64B)) return TOPS_ERR_TMAP;
   }
-  CtArgs args{L, nb, y, Mi, nc, j_begin, j_end};
+  CtArgs args{L, nb, y, Mi, nc, j_begin, j_end, a_groups, b_one};
   static_assert(sizeof(CtSmem) + 1024 <= 227 * 1024, "contraction shared memory");
   const size_t smem = sizeof(CtSmem) + 1024;
   auto kern = trimul_contract_kernel<T, MN>;

@@ -450,6 +450,8 @@ struct CtArgs {
   int Mi;   // rows of A / y (L unsharded; a row slab of size L/P when sharded)
   int nc;   // extent of one B chunk along j (B is P rank-major chunks of nc columns; nc = L unsharded)
   int j_base, j_end;  // the launch computes output columns [j_base, j_end) only (j_base % kCtBN == 0)
+  int a_grouped;      // MN-major A: 1 = a 4-D map whose one box is the whole tile, 0 = one 3-D box per 64 rows
+  int b_one;          // B: 1 = one box per stage (the tile never straddles a chunk), 0 = one per 128 / 64 rows
 };
 
 template <typename T, bool MN>
@@ -505,15 +507,28 @@ __global__ void __launch_bounds__(384, 1)
             tma_load_3d(sm.a[s], &map_a, &sm.full[s], k0, i0, bb);
             // B rows j live in rank-major chunks of nc rows: (j mod nc, chunk j / nc);
             // j >= L lands on chunk >= P, which the tensor map zero-fills.
-            for (int h = 0; h < kCtBN / 128; ++h) {
-              const int j = j0 + h * 128, ch = j / a.nc;
-              tma_load_4d(sm.b[s] + h * 16384, &map_b, &sm.full[s], k0, j - ch * a.nc, bb, ch);
+            if (a.b_one) {
+              const int ch = j0 / a.nc;
+              tma_load_4d(sm.b[s], &map_b, &sm.full[s], k0, j0 - ch * a.nc, bb, ch);
+            } else {
+              for (int h = 0; h < kCtBN / 128; ++h) {
+                const int j = j0 + h * 128, ch = j / a.nc;
+                tma_load_4d(sm.b[s] + h * 16384, &map_b, &sm.full[s], k0, j - ch * a.nc, bb, ch);
+              }
             }
           } else {
-            for (int h = 0; h < kCtBM / 64; ++h) tma_load_3d(sm.a[s] + h * 8192, &map_a, &sm.full[s], i0 + h * 64, k0, bb);
-            for (int h = 0; h < kCtBN / 64; ++h) {
-              const int j = j0 + h * 64, ch = j / a.nc;
-              tma_load_4d(sm.b[s] + h * 8192, &map_b, &sm.full[s], j - ch * a.nc, k0, bb, ch);
+            if (a.a_grouped)
+              tma_load_4d(sm.a[s], &map_a, &sm.full[s], 0, k0, i0 / 64, bb);
+            else
+              for (int h = 0; h < kCtBM / 64; ++h) tma_load_3d(sm.a[s] + h * 8192, &map_a, &sm.full[s], i0 + h * 64, k0, bb);
+            if (a.b_one) {
+              const int ch = j0 / a.nc;
+              tma_load_5d(sm.b[s], &map_b, &sm.full[s], 0, k0, (j0 - ch * a.nc) / 64, bb, ch);
+            } else {
+              for (int h = 0; h < kCtBN / 64; ++h) {
+                const int j = j0 + h * 64, ch = j / a.nc;
+                tma_load_4d(sm.b[s] + h * 8192, &map_b, &sm.full[s], j - ch * a.nc, k0, bb, ch);
+              }
             }
           }
         }
