@@ -292,6 +292,22 @@ def time_op(fn, iters=10, warmup=3):
     return s.elapsed_time(e) / iters
 
 
+def time_graph(fn, iters=50, warmup=3):
+    """Device time of fn replayed from a CUDA graph (captured after warm-up on a side
+    stream): the kernel chain without the host-side launch overhead of the eager call."""
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        fn()
+    return time_op(graph.replay, iters=iters, warmup=warmup)
+
+
 def config3_inputs(dev, L=2048):
     """Config 3 generator: triangle_mul incoming, x~N(0,1) (1, L, L, C) bf16, mask =
     outer(v, v) with v = 1 for the first 1900/2048 of the residues, weights as config 0
@@ -342,10 +358,13 @@ def other_ops(dev):
     pre = tops.attn_pair_bias.precompute(Wq, Wk, Wv, W_ln, B_ln, Wz, None, H, D)
     ms = time_op(lambda: tops.attn_pair_bias.forward(X, Z, pre, scale=1.0, W_proj_g=Wg, B_proj_g=None,
                                                      W_proj_o=Wo, B_proj_o=None, mask=km), iters=50)
+    ms_graph = time_graph(lambda: tops.attn_pair_bias.forward(X, Z, pre, scale=1.0, W_proj_g=Wg, B_proj_g=None,
+                                                              W_proj_o=Wo, B_proj_o=None, mask=km))
     zbytes = M * M * C * 2
     hbm = _peaks()[2]
     out["attention_pair_bias"] = {"config": "M=1024 c_s=C_z=128 bf16, last 64 keys masked", "ms": ms,
-                                  "z_gbs": zbytes / ms / 1e6, "frac_of_hbm": zbytes / ms / 1e6 / hbm}
+                                  "z_gbs": zbytes / ms / 1e6, "frac_of_hbm": zbytes / ms / 1e6 / hbm,
+                                  "ms_cuda_graph": ms_graph, "frac_of_hbm_cuda_graph": zbytes / ms_graph / 1e6 / hbm}
     del X, Z
     out["pairformer_pair_update"] = chain_op(dev)
     return out
