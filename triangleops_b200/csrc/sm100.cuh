@@ -181,7 +181,11 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 #ifndef TOPS_L2_PREFETCH
-#define TOPS_L2_PREFETCH 4  // tiles ahead that the streaming kernels prefetch into L2 (0: off)
+// Tiles ahead that the triangle-mul streaming phases prefetch into L2 (0: off). Off by
+// default: at L = 2048 the input and output phases ran 2 % and 8 % faster without it
+// (0.861 vs 0.877 ms, 0.869 vs 0.950 ms; distances 2 and 8 no better than 4), the whole
+// op 3 % (3.52 vs 3.62 ms, three alternating runs).
+#define TOPS_L2_PREFETCH 0
 #endif
 // Tiled prefetch of a box into L2 (no shared memory, no barrier): a later TMA load of
 // the same box then hits L2. Lets a kernel whose shared-memory ring is shallow keep
