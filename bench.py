@@ -458,6 +458,7 @@ def sharded_ops(dev, world, rank):
             "attn_bias_allgather_ms": tmax(time_op(lambda: tdist.all_gather_rows(
                 torch.empty(H, n, N, dtype=torch.float16, device=dev), 1), iters=10)),
             "chain_transpose_ms": tmax(time_op(lambda: tdist.transpose_rows(x_rows), iters=10)),
+            "chain_column_blocks_ms": tmax(time_op(lambda: tdist.column_blocks(x_rows), iters=10)),
             "bytes_per_rank": {"trimul_b": b.numel() * 2 * (world - 1), "attn_bias": H * n * N * 2 * (world - 1),
                                "transpose": x_rows.numel() * 2 * (world - 1) // world}}
     out["collectives"] = coll

@@ -174,10 +174,11 @@ def _comm_stream(device):
     return _COMM[key]
 
 
-def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
+def _trimul_from_slabs(x_rows, x_cols, pre, direction, mask, eps, group, ops):
     """The triangle multiplicative update of this rank's pair rows from its row slab
-    x_rows (n, L, C) = x[r0:r1] and, for the incoming direction, its column slab given
-    as rows of x^T, x_colsT (n, L, C) = x[:, r0:r1]^T. mask: the full (L, L) mask or None."""
+    x_rows (n, L, C) = x[r0:r1] and, for the incoming direction, its column slab
+    x_cols (L, n, C) = x[:, r0:r1] (any strides; the all-to-all of ``column_blocks``
+    delivers it contiguous). mask: the full (L, L) mask or None."""
     n, L, C = x_rows.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -186,7 +187,7 @@ def _trimul_from_slabs(x_rows, x_colsT, pre, direction, mask, eps, group, ops):
         xs = x_rows.reshape(n * L, C)
         ms = None if mask is None else mask.reshape(L, L)[r0:r1].reshape(n * L)
     else:  # a columns i in slab, b columns j in slab: tokens (k, i)
-        xs = x_colsT.transpose(0, 1).contiguous().reshape(L * n, C)
+        xs = x_cols.contiguous().reshape(L * n, C)
         ms = None if mask is None else mask.reshape(L, L)[:, r0:r1].contiguous().reshape(L * n)
     ab = ops.input_phase(xs.contiguous(), ms, pre, eps)  # (2C, n*L) as [d][i][k] or [d][k][i]
     a = ab[:C].reshape(C, n, L) if direction == "outgoing" else ab[:C].reshape(C, L, n)
@@ -237,8 +238,8 @@ def triangle_multiplicative_update_rows(x, pre, *, direction, mask=None, eps=1e-
         raise ValueError(f"unknown split: {split!r}")
     if world > 1 and split != "rows" and C % world == 0 and hasattr(ops, "contract"):
         return _trimul_channels(x, pre, direction, mask, eps, group, ops, rank, world)
-    x_colsT = None if direction == "outgoing" else x[0, :, r0:r1].transpose(0, 1)
-    return _trimul_from_slabs(x[0, r0:r1], x_colsT, pre, direction, mask, eps, group, ops).unsqueeze(0)
+    x_cols = None if direction == "outgoing" else x[0, :, r0:r1]
+    return _trimul_from_slabs(x[0, r0:r1], x_cols, pre, direction, mask, eps, group, ops).unsqueeze(0)
 
 
 def _trimul_channels(x, pre, direction, mask, eps, group, ops, rank, world):
@@ -260,18 +261,25 @@ def _trimul_channels(x, pre, direction, mask, eps, group, ops, rank, world):
     return out.reshape(1, n, L, C)
 
 
-def transpose_rows(x_rows, group=None):
-    """Rows [r0, r1) of x (n, N, C) -> the same rows of x^T, i.e. x[:, r0:r1]^T (n, N, C),
-    by one all-to-all: rank r sends its (n, n, C) block of columns [j0, j1) to rank j."""
+def column_blocks(x_rows, group=None):
+    """Rows [r0, r1) of x (n, N, C) -> this rank's columns x[:, r0:r1] as a contiguous
+    (world, n, n, C) = [src][i of src's rows][k of my columns][C], i.e. (N, n, C), by one
+    all-to-all: rank r sends its (n, n, C) block of columns [j0, j1) to rank j."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     n, N, C = x_rows.shape
     if world == 1:
-        return x_rows.transpose(0, 1).contiguous()
+        return x_rows.reshape(1, n, N, C)
     assert n * world == N
     send = x_rows.reshape(n, world, n, C).permute(1, 0, 2, 3).contiguous()  # [dest][i][k][C]
-    recv = torch.empty_like(send)  # [src][i of src's rows][k of my columns][C]
+    recv = torch.empty_like(send)
     dist.all_to_all_single(recv.view(-1), send.view(-1), group=group)
-    return recv.permute(2, 0, 1, 3).reshape(n, N, C)  # x^T[k][src * n + i]
+    return recv
+
+
+def transpose_rows(x_rows, group=None):
+    """Rows [r0, r1) of x (n, N, C) -> the same rows of x^T, i.e. x[:, r0:r1]^T (n, N, C)."""
+    n, N, C = x_rows.shape
+    return column_blocks(x_rows, group).permute(2, 0, 1, 3).reshape(n, N, C)  # x^T[k][src * n + i]
 
 
 def pair_update_rows(x_rows, pre, *, mask=None, scale=None, eps=1e-5, group=None, attn_ops=KernelOps,
@@ -288,8 +296,11 @@ def pair_update_rows(x_rows, pre, *, mask=None, scale=None, eps=1e-5, group=None
     r0, r1 = slab(N, rank, world)
     m = None if mask is None else mask.reshape(N, N)
     x_rows = x_rows + _trimul_from_slabs(x_rows, None, pre["tri_mul_out"], "outgoing", m, eps, group, trimul_ops)
-    x_rows = x_rows + _trimul_from_slabs(x_rows, transpose_rows(x_rows, group), pre["tri_mul_in"], "incoming", m, eps,
-                                         group, trimul_ops)
+    # the all-to-all delivers x[:, r0:r1] in exactly the token order the incoming input
+    # phase reads: no transpose copy on either side of it
+    x_cols = column_blocks(x_rows, group).view(N, n, -1)
+    x_rows = x_rows + _trimul_from_slabs(x_rows, x_cols, pre["tri_mul_in"], "incoming", m, eps, group, trimul_ops)
+    del x_cols
     for name, ending in (("tri_attn_start", False), ("tri_attn_end", True)):
         p = pre[name]
         sc = p["D"] ** -0.5 if scale is None else scale
@@ -297,7 +308,13 @@ def pair_update_rows(x_rows, pre, *, mask=None, scale=None, eps=1e-5, group=None
         mr = None if m is None else (m.t() if ending else m)[r0:r1].contiguous()
         o = triangle_attention_rows(src.contiguous(), p, N=N, mask_rows=mr, scale=sc, eps=eps,
                                     W_proj_g=p["W_proj_g"], W_proj_o=p["W_proj_o"], group=group, ops=attn_ops)
-        x_rows = x_rows + (transpose_rows(o, group) if ending else o)
+        if ending:
+            # x[i][src*n + k] += o^T: added through a permuted view of the received blocks,
+            # in place (x_rows is this function's own tensor by now), without a transpose copy
+            blk = column_blocks(o, group)  # [src][k of src's rows][i of mine][C]
+            x_rows.view(n, world, n, -1).add_(blk.permute(2, 0, 1, 3))
+        else:
+            x_rows = x_rows + o
     return x_rows
 
 
