@@ -333,3 +333,44 @@ def test_sharded_pairformer_chain_gloo():
     x, w, mask = _chain_inputs()
     ref = oracle.pair_update(x, mask=mask, **w)
     assert (full - ref).abs().max().item() < 1e-4
+
+
+def _blocks_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N, C = 6 * world, 3
+        x = torch.arange(N * N * C, dtype=torch.float32).reshape(N, N, C)
+        r0, r1 = tdist.slab(N, rank, world)
+        blk = tdist.column_blocks(x[r0:r1].contiguous())
+        ok_cols = torch.equal(blk.reshape(N, r1 - r0, C), x[:, r0:r1])
+        ok_t = torch.equal(tdist.transpose_rows(x[r0:r1].contiguous()), x.transpose(0, 1)[r0:r1])
+        # the chain's in-place add of an ending-node result o (rows of the transposed
+        # problem) through a permuted view of its column blocks
+        o = -x.transpose(0, 1).contiguous()
+        acc = x[r0:r1].clone()
+        n = r1 - r0
+        acc.view(n, world, n, C).add_(tdist.column_blocks(o[r0:r1].contiguous()).permute(2, 0, 1, 3))
+        ok_add = torch.equal(acc, x[r0:r1] + o.transpose(0, 1)[r0:r1])
+        q.put((rank, ok_cols, ok_t, ok_add))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_column_blocks_gloo(world):
+    """column_blocks delivers x[:, r0:r1] as (N, n, C) in the receive buffer's own layout,
+    transpose_rows the rows of x^T, and the permuted in-place add used for the ending node
+    equals adding the transposed result."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_blocks_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok_cols and ok_t and ok_add for _, ok_cols, ok_t, ok_add in res), res
